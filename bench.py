@@ -1,0 +1,313 @@
+"""Headline benchmark: DDP training throughput with 4-bit error-feedback
+low-bit gradient all-reduce.
+
+Config: ResNet-18 CIFAR-style (3x3 stem, no max-pool,
+10-way head), DDP with the low-bit comm hook at 4-bit + error feedback, bf16
+autocast, SGD momentum 0.9, synthetic 32x32x3 fp32 images ~N(0,1) with labels
+uniform over 10 classes, batch 256 per GPU, seed 0.  Weak scaling: every GPU
+trains on its own 256 images per step.
+
+    python bench.py --gpus 1 --steps 20 --warmup 5
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \
+        --master-port 29500 bench.py --gpus 8 --steps 20 --warmup 5
+    python bench.py --impl reference ...      # the reference package, same config
+
+Reported (rank 0, one JSON line):
+  value      samples/s of the whole job, device-timed with CUDA events over K
+             steps with inputs resident on the device (rotating pool larger
+             than L2), max over ranks;
+  e2e.value  samples/s through the same public API with, every step, an H2D
+             copy of the batch from pinned host memory and a D2H read of the
+             loss, also device-timed and max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "DDP samples/s (ResNet-18 CIFAR, 4-bit EF low-bit all-reduce)"
+BASELINE_VALUE = None  # the reference publishes no ResNet-18 DDP number
+L2_BYTES = 126 * 2**20
+POOL = 48  # distinct input batches cycled through (48 x 3 MiB > L2)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=256)
+    p.add_argument("--bits", type=int, default=4)
+    p.add_argument("--bucket-mb", type=float, default=25.0)
+    p.add_argument("--max-ctas", type=int, default=0)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------
+def setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    torch.cuda.set_device(local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29517")
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier_sync(world):
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def make_data(rank, batch, device):
+    g = torch.Generator().manual_seed(0 + rank)
+    xs = torch.randn(POOL, batch, 3, 32, 32, generator=g)
+    ys = torch.randint(0, 10, (POOL, batch), generator=g)
+    return xs, ys
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+def build_ours(args, rank, world, local):
+    sys.path.insert(0, ROOT)
+    import bitscom_b200 as bitscom
+    from bitscom_b200.models import resnet18_cifar
+
+    kw = {} if world > 1 else {"init_method": "tcp://127.0.0.1:%s" % os.environ["MASTER_PORT"], "rank": 0, "world_size": 1}
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local), **kw)
+    torch.manual_seed(0)
+    model = resnet18_cifar(10).cuda().to(memory_format=torch.channels_last)
+    ddp = nn.parallel.DistributedDataParallel(
+        model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True,
+        process_group=dist.group.WORLD,
+    )
+    state = bitscom.register_lowbit_hook(ddp, bitwidth=args.bits, error_feedback=True, max_ctas=args.max_ctas)
+    opt = torch.optim.SGD(ddp.parameters(), lr=0.1, momentum=0.9, fused=True)
+
+    def step(x, y):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = F.cross_entropy(ddp(x), y)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        return loss
+
+    def launches():
+        n = 0
+        for c in state._comms.values():
+            if c is not None:
+                n += c.stats()["launches"]
+        return n
+
+    return step, launches, "bitscom_b200 DDP comm hook (fused sm_100a NVLink kernel)"
+
+
+# ----------------------------------------------------------------------------
+# reference arm: the unmodified reference package from baseline/_ref
+# ----------------------------------------------------------------------------
+def build_reference(args, rank, world, local):
+    ref_path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_path, "bitscom")):
+        return None, None, "reference not installed in baseline/_ref"
+    sys.path.insert(0, ref_path)
+    import bitscom  # the reference package
+    import torchvision
+
+    bitscom.init(bitwidth=args.bits, error_feedback=True)
+    if world > 1:
+        dist.init_process_group("lowbit", timeout=datetime.timedelta(seconds=120))
+    else:
+        dist.init_process_group("lowbit", init_method="tcp://127.0.0.1:%s" % os.environ["MASTER_PORT"], rank=0, world_size=1)
+    torch.manual_seed(0)
+    model = torchvision.models.resnet18(num_classes=10)
+    model.conv1 = nn.Conv2d(3, 64, 3, 1, 1, bias=False)
+    model.maxpool = nn.Identity()
+    model = model.cuda().to(memory_format=torch.channels_last)
+    for p in model.parameters():  # same initial weights on every rank
+        dist.broadcast(p.data, 0)
+    opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9)
+    params = [p for p in model.parameters()]
+    # Persistent flat buckets (so the reference's TensorImpl-keyed EF residual
+    # persists across steps), padded to a multiple of world size as its C++
+    # path requires; gradients are all-reduced through dist.all_reduce on the
+    # lowbit process group, the reference's error-feedback path.
+    cap = int(args.bucket_mb * 2**20 / 4)
+    buckets, cur, size = [], [], 0
+    for p in reversed(params):
+        if cur and size + p.numel() > cap:
+            buckets.append(cur)
+            cur, size = [], 0
+        cur.append(p)
+        size += p.numel()
+    if cur:
+        buckets.append(cur)
+    flats = []
+    for b in buckets:
+        n = sum(p.numel() for p in b)
+        n += (-n) % world
+        flats.append(torch.zeros(n, device="cuda"))
+
+    def step(x, y):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = F.cross_entropy(model(x), y)
+        loss.backward()
+        for b, flat in zip(buckets, flats):
+            off = 0
+            for p in b:
+                flat[off : off + p.numel()].copy_(p.grad.view(-1))
+                off += p.numel()
+            dist.all_reduce(flat).wait()
+            flat.div_(world)
+            off = 0
+            for p in b:
+                p.grad.copy_(flat[off : off + p.numel()].view_as(p.grad))
+                off += p.numel()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        return loss
+
+    return step, (lambda: 0), "reference bitscom lowbit backend (dist.all_reduce, C++ EF path)"
+
+
+# ----------------------------------------------------------------------------
+def timed(step, xs_dev, ys_dev, steps, world, e2e_host=None):
+    """Device-timed K steps; with e2e_host=(xs_pinned, ys_pinned) each step
+    copies its batch H2D from pinned memory and reads the loss back D2H."""
+    loss_host = torch.empty(steps, dtype=torch.float32, pin_memory=True)
+    xbuf = torch.empty_like(xs_dev[0])
+    ybuf = torch.empty_like(ys_dev[0])
+    barrier_sync(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        j = i % POOL
+        if e2e_host is not None:
+            xbuf.copy_(e2e_host[0][j], non_blocking=True)
+            ybuf.copy_(e2e_host[1][j], non_blocking=True)
+            loss = step(xbuf.contiguous(memory_format=torch.channels_last), ybuf)
+            loss_host[i : i + 1].copy_(loss.detach().float().view(1), non_blocking=True)
+        else:
+            step(xs_dev[j].contiguous(memory_format=torch.channels_last), ys_dev[j])
+    t1.record()
+    barrier_sync(world)
+    ms = t0.elapsed_time(t1)
+    if e2e_host is not None:
+        assert torch.isfinite(loss_host).all(), "non-finite loss"
+    return ms, loss_host
+
+
+def main():
+    args = parse()
+    rank, world, local = setup(args)
+    if args.impl == "reference":
+        try:
+            step, launches, desc = build_reference(args, rank, world, local)
+        except Exception as exc:  # pragma: no cover - depends on the reference build
+            step, desc = None, f"reference failed to start: {exc!r}"[:300]
+        if step is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": desc}))
+            return
+    else:
+        step, launches, desc = build_ours(args, rank, world, local)
+
+    xs, ys = make_data(rank, args.batch, "cuda")
+    xs_dev, ys_dev = xs.cuda(), ys.cuda()
+    xs_pin, ys_pin = xs.pin_memory(), ys.pin_memory()
+
+    for i in range(args.warmup):
+        step(xs_dev[i % POOL].contiguous(memory_format=torch.channels_last), ys_dev[i % POOL])
+    barrier_sync(world)
+
+    from bitscom_b200.utils.clocks import ClockSampler
+
+    l0 = launches()
+    with ClockSampler(list(range(world)) if rank == 0 else [local]) as cs:
+        ms, _ = timed(step, xs_dev, ys_dev, args.steps, world)
+    l1 = launches()
+    ms = max_over_ranks(ms, world)
+    e2e = None
+    if not args.no_e2e:
+        ms_e2e, _ = timed(step, xs_dev, ys_dev, args.steps, world, e2e_host=(xs_pin, ys_pin))
+        ms_e2e = max_over_ranks(ms_e2e, world)
+        img_bytes = xs[0].numel() * xs.element_size() + ys[0].numel() * ys.element_size()
+        e2e = {
+            "value": round(args.batch * world * args.steps / (ms_e2e / 1e3), 2),
+            "unit": "samples/s",
+            "ms_per_step": round(ms_e2e / args.steps, 4),
+            "h2d_bytes_per_step": int(img_bytes),
+            "d2h_bytes_per_step": 4,
+        }
+    value = args.batch * world * args.steps / (ms / 1e3)
+    clocks = cs.summary()
+    if rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "samples/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
+            "dtype": "bf16",
+            "data": "synthetic (N(0,1) 32x32x3 images, uniform labels; random-init weights)",
+            "config": {
+                "model": "resnet18_cifar",
+                "global_batch": args.batch * world,
+                "per_gpu_batch": args.batch,
+                "seq_len": None,
+                "image": [3, 32, 32],
+                "parallelism": f"dp{world}",
+                "comm": f"{args.bits}-bit error-feedback low-bit all-reduce, {args.bucket_mb} MB buckets",
+                "optimizer": "SGD momentum 0.9",
+                "l2": f"rotating pool of {POOL} device-resident batches ({POOL * 3} MiB > 126 MiB L2)",
+                "implementation": desc,
+            },
+            "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"), "reasons": clocks.get("reasons")},
+            "gpu_launches": int(l1 - l0),
+        }
+        if args.impl == "reference":
+            out["impl"] = "reference"
+        if e2e is not None:
+            out["e2e"] = e2e
+        print(json.dumps(out), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

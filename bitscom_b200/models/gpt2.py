@@ -1,0 +1,105 @@
+"""GPT-2 (decoder-only transformer) for the sharded data-parallel benchmark.
+
+Architecture of GPT-2: learned token + position embeddings, pre-LayerNorm
+blocks (causal multi-head attention, 4x GELU MLP), final LayerNorm, LM head
+tied to the token embedding.  Attention uses
+``F.scaled_dot_product_attention`` (flash kernels under bf16).  The reference
+used Hugging Face's GPT2LMHeadModel with a 4-layer/256-wide config (reference
+benchmarks/multimodel_stochastic_e2e_curve.py:62-74); :func:`gpt2_medium` is
+the 24-layer / 1024-wide / 16-head model of the sharded benchmark config.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+@dataclass
+class GPT2Config:
+    vocab_size: int = 50257
+    n_positions: int = 1024
+    n_embd: int = 1024
+    n_layer: int = 24
+    n_head: int = 16
+    dropout: float = 0.0
+
+
+class _Attention(nn.Module):
+    def __init__(self, cfg: GPT2Config):
+        super().__init__()
+        self.n_head = cfg.n_head
+        self.qkv = nn.Linear(cfg.n_embd, 3 * cfg.n_embd)
+        self.proj = nn.Linear(cfg.n_embd, cfg.n_embd)
+
+    def forward(self, x):
+        b, t, c = x.shape
+        q, k, v = self.qkv(x).split(c, dim=2)
+        shape = (b, t, self.n_head, c // self.n_head)
+        q, k, v = (z.view(shape).transpose(1, 2) for z in (q, k, v))
+        y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return self.proj(y.transpose(1, 2).reshape(b, t, c))
+
+
+class _Block(nn.Module):
+    def __init__(self, cfg: GPT2Config):
+        super().__init__()
+        self.ln1 = nn.LayerNorm(cfg.n_embd)
+        self.attn = _Attention(cfg)
+        self.ln2 = nn.LayerNorm(cfg.n_embd)
+        self.fc = nn.Linear(cfg.n_embd, 4 * cfg.n_embd)
+        self.out = nn.Linear(4 * cfg.n_embd, cfg.n_embd)
+
+    def forward(self, x):
+        x = x + self.attn(self.ln1(x))
+        return x + self.out(F.gelu(self.fc(self.ln2(x)), approximate="tanh"))
+
+
+class GPT2(nn.Module):
+    def __init__(self, cfg: GPT2Config):
+        super().__init__()
+        self.cfg = cfg
+        self.wte = nn.Embedding(cfg.vocab_size, cfg.n_embd)
+        self.wpe = nn.Embedding(cfg.n_positions, cfg.n_embd)
+        self.blocks = nn.ModuleList([_Block(cfg) for _ in range(cfg.n_layer)])
+        self.ln_f = nn.LayerNorm(cfg.n_embd)
+        self.apply(self._init)
+        for name, p in self.named_parameters():
+            if name.endswith("proj.weight") or name.endswith("out.weight"):
+                nn.init.normal_(p, 0.0, 0.02 / math.sqrt(2 * cfg.n_layer))
+
+    @staticmethod
+    def _init(m):
+        if isinstance(m, nn.Linear):
+            nn.init.normal_(m.weight, 0.0, 0.02)
+            if m.bias is not None:
+                nn.init.zeros_(m.bias)
+        elif isinstance(m, nn.Embedding):
+            nn.init.normal_(m.weight, 0.0, 0.02)
+
+    def forward(self, idx: torch.Tensor, targets: torch.Tensor | None = None):
+        t = idx.shape[1]
+        pos = torch.arange(t, device=idx.device)
+        x = self.wte(idx) + self.wpe(pos)
+        for blk in self.blocks:
+            x = blk(x)
+        logits = F.linear(self.ln_f(x), self.wte.weight)
+        if targets is None:
+            return logits
+        loss = F.cross_entropy(logits.float().view(-1, logits.size(-1)), targets.view(-1))
+        return logits, loss
+
+
+def gpt2_medium(**overrides) -> GPT2:
+    return GPT2(GPT2Config(**overrides))
+
+
+def gpt2_small_test(**overrides) -> GPT2:
+    """4-layer, 256-wide GPT-2 (the reference's benchmark size)."""
+    cfg = dict(n_embd=256, n_layer=4, n_head=4, n_positions=512)
+    cfg.update(overrides)
+    return GPT2(GPT2Config(**cfg))

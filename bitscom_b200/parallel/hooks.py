@@ -1,0 +1,183 @@
+"""DDP communication hook running the fused low-bit all-reduce per bucket.
+
+The reference has no DDP integration: its benchmarks all-reduce a hand-built
+bucket after ``backward()`` with no overlap (reference
+benchmarks/multimodel_stochastic_e2e_curve.py:207-244), and DDP on its
+``lowbit`` backend would lose the second phase through the Work future bug
+(cpp/src/process_group_lowbit.cc:42-44).
+
+Here DDP calls :func:`lowbit_allreduce_hook` as soon as a bucket's gradients
+are ready, during backward.  The hook enqueues ONE fused kernel on a dedicated
+communication stream (ordered after the gradient producers), so the low-bit
+all-reduce of bucket k overlaps the backward kernels of buckets k+1..; the
+returned CUDA-aware future completes in stream order.  Gradients are averaged
+inside the kernel (``post_scale = 1/world``), the error-feedback residual of
+each bucket lives in :class:`LowBitHookState` (keyed by bucket index, shape
+checked) and is checkpointable through ``state_dict()``.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from .comm import Communicator
+
+
+class LowBitHookState:
+    """State of :func:`lowbit_allreduce_hook`.
+
+    Args:
+        process_group: group to reduce over (default: the default group).
+        bitwidth: wire bitwidth (1, 2, 4, 8, 12, 16).
+        error_feedback: keep a per-bucket fp32 residual.
+        stochastic_rounding: Philox stochastic rounding of the first quantisation.
+        fp8: 8-bit buckets use the block-scaled E4M3 wire format.
+        algo: "auto", "oneshot" or "twoshot".
+        max_ctas: CTAs of each fused launch (0 = one per SM); fewer leave SMs
+            to the overlapping backward kernels.
+        compress_single_rank: at world size 1 still run the (loopback) kernel,
+            so a 1-GPU run applies exactly the quantisation an N-GPU run does.
+        seed: Philox key of stochastic rounding.
+    """
+
+    def __init__(
+        self,
+        process_group: Optional[dist.ProcessGroup] = None,
+        bitwidth: int = 4,
+        error_feedback: bool = True,
+        stochastic_rounding: bool = False,
+        fp8: bool = False,
+        algo: str = "auto",
+        max_ctas: int = 0,
+        compress_single_rank: bool = True,
+        seed: int = 0x5EED,
+        use_comm_stream: bool = True,
+    ):
+        if bitwidth not in (1, 2, 4, 8, 12, 16):
+            raise ValueError(f"bitwidth must be one of (1, 2, 4, 8, 12, 16), got {bitwidth}")
+        self.process_group = process_group
+        self.bitwidth = bitwidth
+        self.error_feedback = error_feedback
+        self.stochastic_rounding = stochastic_rounding
+        self.fp8 = fp8 and bitwidth == 8
+        self.algo = algo
+        self.max_ctas = max_ctas
+        self.compress_single_rank = compress_single_rank
+        self.seed = int(seed)
+        self.use_comm_stream = use_comm_stream
+        self.calls = 0
+        self.residuals: Dict[int, torch.Tensor] = {}
+        self._comms: Dict[int, Optional[Communicator]] = {}
+        self._streams: Dict[int, torch.cuda.Stream] = {}
+
+    # ------------------------------------------------------------ plumbing
+    @property
+    def world_size(self) -> int:
+        return dist.get_world_size(self.process_group)
+
+    def communicator(self, device: torch.device) -> Optional[Communicator]:
+        idx = device.index
+        if idx not in self._comms:
+            if self.world_size == 1:
+                self._comms[idx] = Communicator.create_local(idx)
+            else:
+                self._comms[idx] = Communicator.for_group(self.process_group, idx)
+        return self._comms[idx]
+
+    def stream(self, device: torch.device) -> torch.cuda.Stream:
+        idx = device.index
+        if idx not in self._streams:
+            self._streams[idx] = torch.cuda.Stream(device=device, priority=-1)
+        return self._streams[idx]
+
+    def residual(self, bucket_index: int, buf: torch.Tensor) -> Optional[torch.Tensor]:
+        if not self.error_feedback:
+            return None
+        r = self.residuals.get(bucket_index)
+        if r is not None and r.numel() == buf.numel() and r.device != buf.device:
+            r = self.residuals[bucket_index] = r.to(buf.device, torch.float32).contiguous()
+        if r is None or r.numel() != buf.numel():
+            r = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device)
+            self.residuals[bucket_index] = r
+        return r
+
+    # ---------------------------------------------------------- checkpoint
+    def state_dict(self) -> dict:
+        return {
+            "calls": self.calls,
+            "bitwidth": self.bitwidth,
+            "residuals": {k: v.detach().cpu().clone() for k, v in self.residuals.items()},
+        }
+
+    def load_state_dict(self, state: dict) -> None:
+        if int(state.get("bitwidth", self.bitwidth)) != self.bitwidth:
+            raise ValueError("checkpoint was written with a different bitwidth")
+        self.calls = int(state.get("calls", 0))
+        self.residuals = {int(k): v.clone() for k, v in state.get("residuals", {}).items()}
+
+
+def _staged_fallback(state: LowBitHookState, buf: torch.Tensor) -> torch.Tensor:
+    from ..api import LowBitGroup
+
+    grp = LowBitGroup(state.bitwidth, process_group=state.process_group,
+                      stochastic_rounding=state.stochastic_rounding, use_fused=False)
+    out = grp._staged_allreduce(buf.view(-1), state.process_group, None)
+    return out.div_(state.world_size).to(buf.dtype)
+
+
+def lowbit_allreduce_hook(state: LowBitHookState, bucket) -> torch.futures.Future:
+    """DDP comm hook: fused low-bit all-reduce (mean) of ``bucket.buffer()``."""
+    buf = bucket.buffer()
+    world = state.world_size
+    state.calls += 1
+    if not buf.is_cuda or (world == 1 and not state.compress_single_rank):
+        fut = torch.futures.Future()
+        if world > 1:
+            fut.set_result(_staged_fallback(state, buf))
+        else:
+            fut.set_result(buf)
+        return fut
+
+    comm = state.communicator(buf.device)
+    if comm is None:  # no peer access: staged path on the current stream
+        fut = torch.futures.Future(devices=[buf.device])
+        fut.set_result(_staged_fallback(state, buf))
+        return fut
+
+    residual = state.residual(bucket.index(), buf)
+    cur = torch.cuda.current_stream(buf.device)
+    stream = state.stream(buf.device) if state.use_comm_stream else cur
+    if stream is not cur:
+        stream.wait_stream(cur)
+    with torch.cuda.stream(stream):
+        comm.all_reduce(
+            buf,
+            bits=state.bitwidth,
+            fmt="e4m3" if state.fp8 else "int",
+            residual=residual,
+            stochastic_rounding=state.stochastic_rounding,
+            stochastic_requant=state.stochastic_rounding,
+            seed=state.seed,
+            offset=state.calls,
+            post_scale=1.0 / world,
+            algo=state.algo,
+            max_ctas=state.max_ctas,
+        )
+        fut = torch.futures.Future(devices=[buf.device])
+        fut.set_result(buf)
+    if stream is not cur:
+        buf.record_stream(stream)
+        if residual is not None:
+            residual.record_stream(stream)
+    return fut
+
+
+def register_lowbit_hook(ddp_model, **kwargs) -> LowBitHookState:
+    """Create a :class:`LowBitHookState` and register the hook on a DDP model."""
+    pg = kwargs.pop("process_group", None) or ddp_model.process_group
+    state = LowBitHookState(process_group=pg, **kwargs)
+    ddp_model.register_comm_hook(state, lowbit_allreduce_hook)
+    return state

@@ -1,0 +1,573 @@
+// Fused low-bit collectives over NVLink-5 / NVSwitch peer memory (sm_100a).
+//
+// One kernel launch performs an entire collective:
+//
+//   two-shot all-reduce  (replaces reference python/bitscom/api.py:179-257 and
+//                         cpp/src/process_group_lowbit.cc:153-328 with their
+//                         4 NCCL calls, >=2W+1 host syncs and ~6W ATen launches)
+//     phase 1  for every destination shard d: read g (fp32|bf16), add the
+//              error-feedback residual, block absmax, quantise (Philox SR),
+//              pack, STORE the packed sub-chunk straight into rank d's
+//              receive slot over NVLink, write the new residual, signal d.
+//     phase 2  (owner) wait for all W packed contributions of one chunk of its
+//              shard, dequantise + sum in fp32 in rank order, requantise,
+//              pack, STORE the packed result into every rank's gather slot,
+//              write its own output, signal every rank.
+//     phase 3  wait for each owner's packed chunk, unpack + dequantise into
+//              the output.
+//   one-shot all-reduce  phase 1 broadcasts the whole packed tensor; phase 2
+//                        dequantise-sums all W contributions (no requantisation).
+//   reduce-scatter       phases 1+2, fp output shard.
+//   all-gather           quantise own shard once, broadcast, unpack all shards.
+//
+// Work distribution is a per-launch ticket counter: CTAs claim items in
+// phase order (all phase-1 items are claimed before any phase-2 item, ...).
+// Phase-1 items never wait, so every wait depends only on items that have
+// already been claimed by running CTAs; the kernel therefore cannot deadlock
+// even when only part of its grid is resident (e.g. sharing SMs with backward
+// kernels), which a static CTA->chunk mapping would not guarantee.
+//
+// Every wait is bounded by %globaltimer: on expiry the CTA records
+// kStatusTimeout in a host-mapped status word, raises a launch-local abort
+// flag that makes the other CTAs drain, and returns normally (no trap).
+//
+// Wire format (internal; compress() keeps the reference layout): 1024-element
+// blocks with one fp32 scale each; lane l of a warp owns elements
+// (k*32+l)*4+m (k<8, m<4) of the block, so input loads are fully coalesced
+// 128-bit loads and each lane emits exactly `bits` 32-bit words with no
+// shared-memory transpose.  Eight blocks form a sub-chunk:
+//   [8 x fp32 scales][8 x 128*bits bytes payload].
+// Payload words are interleaved across lanes in 16-byte vectors so every
+// store/load instruction of a warp covers a contiguous span.
+#include "coll_params.h"
+#include "common.cuh"
+#include "launchers.h"
+
+#include <cuda_fp8.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace bitscom {
+namespace {
+
+constexpr int kThreads = 256;  // 8 warps = one sub-chunk per CTA pass
+
+// ---------------------------------------------------------------------------
+// Element access in the interleaved block mapping.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load_block(const T* __restrict__ p, int64_t blk_base, int64_t n,
+                                           bool vec, int lane, float (&v)[32]) {
+  if (vec && blk_base + kBlockElems <= n) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float t[4];
+      ElemIO<T>::load4(p + blk_base + (k * 32 + lane) * 4, t);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) v[k * 4 + m] = t[m];
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int64_t e = blk_base + (k * 32 + lane) * 4 + m;
+        v[k * 4 + m] = (e < n) ? ElemIO<T>::load(p + e) : 0.0f;
+      }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_block(T* __restrict__ p, int64_t blk_base, int64_t n,
+                                            bool vec, int lane, const float (&v)[32]) {
+  if (vec && blk_base + kBlockElems <= n) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float t[4] = {v[k * 4], v[k * 4 + 1], v[k * 4 + 2], v[k * 4 + 3]};
+      ElemIO<T>::store4(p + blk_base + (k * 32 + lane) * 4, t);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int64_t e = blk_base + (k * 32 + lane) * 4 + m;
+        if (e < n) ElemIO<T>::store(p + e, v[k * 4 + m]);
+      }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Codecs.  encode(): 32 values + block scale -> 32 codes; decode(): inverse.
+// ---------------------------------------------------------------------------
+template <int B, int FMT>
+struct Codec;
+
+template <int B>
+struct Codec<B, kFmtInt> {
+  static constexpr int qmin = QBounds<B>::qmin;
+  static constexpr int qmax = QBounds<B>::qmax;
+  __device__ __forceinline__ static float scale_of(float amax) {
+    return amax > 0.0f ? amax / static_cast<float>(qmax) : 1.0f;
+  }
+  // Returns the dequantised value of each code in `deq`.
+  // SR draws come from Philox(counter = {element/4 ^ stream<<52, offset}, key = seed);
+  // stream = phase + 4*rank keeps ranks and phases independent.
+  __device__ __forceinline__ static void encode(const float (&v)[32], float scale, bool sr,
+                                                uint64_t grp0, uint32_t stream, uint64_t seed,
+                                                uint64_t offset, uint32_t (&codes)[32],
+                                                float (&deq)[32]) {
+    const float inv = 1.0f / scale;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      Philox4 r{0u, 0u, 0u, 0u};
+      if (sr) {
+        Philox4 c;
+        const uint64_t g = grp0 + k * 32;
+        c.x = static_cast<uint32_t>(g);
+        c.y = static_cast<uint32_t>(g >> 32) ^ (stream << 20);
+        c.z = static_cast<uint32_t>(offset);
+        c.w = static_cast<uint32_t>(offset >> 32);
+        r = philox4x32_10(c, static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
+      }
+      const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float x = v[k * 4 + m] * inv;
+        float q = sr ? sr_round(x, rr[m]) : rintf(x);
+        q = fminf(fmaxf(q, static_cast<float>(qmin)), static_cast<float>(qmax));
+        codes[k * 4 + m] = static_cast<uint32_t>(static_cast<int>(q) - qmin);
+        deq[k * 4 + m] = q * scale;
+      }
+    }
+  }
+  __device__ __forceinline__ static float decode(uint32_t code, float scale) {
+    return static_cast<float>(static_cast<int>(code) + qmin) * scale;
+  }
+};
+
+template <int B>
+struct Codec<B, kFmtE4M3> {
+  static_assert(B == 8, "E4M3 codes are 8 bits");
+  __device__ __forceinline__ static float scale_of(float amax) {
+    return amax > 0.0f ? amax / 448.0f : 1.0f;
+  }
+  __device__ __forceinline__ static void encode(const float (&v)[32], float scale, bool,
+                                                uint64_t, uint32_t, uint64_t, uint64_t,
+                                                uint32_t (&codes)[32], float (&deq)[32]) {
+    const float inv = 1.0f / scale;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const float2 f = make_float2(v[j] * inv, v[j + 1] * inv);
+      const __nv_fp8x2_storage_t c2 = __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
+      codes[j] = c2 & 0xffu;
+      codes[j + 1] = (c2 >> 8) & 0xffu;
+      deq[j] = decode(codes[j], scale);
+      deq[j + 1] = decode(codes[j + 1], scale);
+    }
+  }
+  __device__ __forceinline__ static float decode(uint32_t code, float scale) {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
+    return __half2float(__half(h)) * scale;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Packed sub-chunk I/O.  Lane-interleaved payload: vector r of lane l sits at
+// vector index r*32 + l.
+// ---------------------------------------------------------------------------
+template <int B>
+__device__ __forceinline__ void put_words(uint8_t* sub, int blk, int lane, const uint32_t (&w)[B]) {
+  uint8_t* pay = sub + kHeaderBytes + blk * 128 * B;
+  if constexpr (B % 4 == 0) {
+#pragma unroll
+    for (int r = 0; r < B / 4; ++r)
+      *reinterpret_cast<uint4*>(pay + (r * 32 + lane) * 16) =
+          make_uint4(w[4 * r], w[4 * r + 1], w[4 * r + 2], w[4 * r + 3]);
+  } else if constexpr (B == 2) {
+    *reinterpret_cast<uint2*>(pay + lane * 8) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(pay + lane * 4) = w[0];
+  }
+}
+
+template <int B>
+__device__ __forceinline__ void get_words(const uint8_t* sub, int blk, int lane, uint32_t (&w)[B]) {
+  const uint8_t* pay = sub + kHeaderBytes + blk * 128 * B;
+  if constexpr (B % 4 == 0) {
+#pragma unroll
+    for (int r = 0; r < B / 4; ++r) {
+      const uint4 t = __ldcg(reinterpret_cast<const uint4*>(pay + (r * 32 + lane) * 16));
+      w[4 * r] = t.x; w[4 * r + 1] = t.y; w[4 * r + 2] = t.z; w[4 * r + 3] = t.w;
+    }
+  } else if constexpr (B == 2) {
+    const uint2 t = __ldcg(reinterpret_cast<const uint2*>(pay + lane * 8));
+    w[0] = t.x; w[1] = t.y;
+  } else {
+    w[0] = __ldcg(reinterpret_cast<const uint32_t*>(pay + lane * 4));
+  }
+}
+
+__device__ __forceinline__ float get_scale(const uint8_t* sub, int blk) {
+  return __ldcg(reinterpret_cast<const float*>(sub) + blk);
+}
+
+__device__ __forceinline__ void put_scale(uint8_t* sub, int blk, float s) {
+  reinterpret_cast<float*>(sub)[blk] = s;
+}
+
+// ---------------------------------------------------------------------------
+// Workspace addressing.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint8_t* rs_sub(const CollParams& p, int rank_base, int slot, int64_t sub) {
+  return p.peer_base[rank_base] + p.rs_data_off[p.parity] + (slot * p.slot_subs + sub) * p.sub_bytes;
+}
+__device__ __forceinline__ uint8_t* ag_sub(const CollParams& p, int rank_base, int slot, int64_t sub) {
+  return p.peer_base[rank_base] + p.ag_data_off[p.parity] + (slot * p.slot_subs + sub) * p.sub_bytes;
+}
+__device__ __forceinline__ uint32_t* rs_flag(const CollParams& p, int rank_base, int slot, int64_t item) {
+  return reinterpret_cast<uint32_t*>(p.peer_base[rank_base] + p.rs_flag_off[p.parity]) +
+         slot * p.slot_items + item;
+}
+__device__ __forceinline__ uint32_t* ag_flag(const CollParams& p, int rank_base, int slot, int64_t item) {
+  return reinterpret_cast<uint32_t*>(p.peer_base[rank_base] + p.ag_flag_off[p.parity]) +
+         slot * p.slot_items + item;
+}
+
+// ---------------------------------------------------------------------------
+// Bounded wait (one thread).  Returns false on timeout or launch abort.
+// ---------------------------------------------------------------------------
+__device__ bool wait_epoch(const CollParams& p, const uint32_t* flag) {
+  if (ld_acquire_sys(flag) == p.epoch) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (ld_acquire_sys(flag) == p.epoch) return true;
+    if ((++spins & 63u) == 0u) {
+      if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) return false;
+      if (globaltimer_ns() - t0 > p.timeout_ns) {
+        // Host-mapped status: a plain system-scope store (device atomics on
+        // host memory are not available on every platform).
+        *reinterpret_cast<volatile uint32_t*>(p.status) = kStatusTimeout;
+        atomicExch(p.abort_flag, 1u);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ void signal(const CollParams& p, uint32_t* flag) {
+  if (p.fault_skip != nullptr && *p.fault_skip != 0u) return;  // test hook: drop the signal
+  st_release_sys(flag, p.epoch);
+}
+
+// Thread 0 waits on every flag in flags[0..count) (stride `stride` words);
+// the verdict is broadcast to the CTA.
+__device__ bool cta_wait(const CollParams& p, uint32_t* const* flags, int count, bool* ok_smem) {
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int i = 0; i < count && ok; ++i) ok = wait_epoch(p, flags[i]);
+    *ok_smem = ok;
+  }
+  __syncthreads();
+  const bool ok = *ok_smem;
+  __syncthreads();
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
+// The kernel.
+// ---------------------------------------------------------------------------
+template <typename T, int B, int FMT>
+__global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_constant__ CollParams p) {
+  using C = Codec<B, FMT>;
+  __shared__ uint32_t s_item;
+  __shared__ bool s_ok;
+  __shared__ uint32_t* s_flags[kMaxRanks];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int W = p.world;
+  const int me = p.rank;
+  const int64_t IS = p.n_items_slot;
+  const bool vec_in = (reinterpret_cast<uintptr_t>(p.in) & 15u) == 0;
+  const bool vec_out = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
+  const bool vec_res = (reinterpret_cast<uintptr_t>(p.residual) & 15u) == 0;
+  const T* in = static_cast<const T*>(p.in);
+  T* out = static_cast<T*>(p.out);
+  // All-gather output slices start at src * n elements: vector stores only
+  // when that offset keeps 16-byte alignment.
+  auto vec_ag = [&](int src) {
+    return vec_out && ((static_cast<int64_t>(src) * p.n * static_cast<int64_t>(sizeof(T))) & 15) == 0;
+  };
+
+  // Phase sizes.
+  int64_t n1, n2, n3;
+  switch (p.op) {
+    case kAllReduceTwoShot: n1 = W * IS; n2 = IS; n3 = (W - 1) * IS; break;
+    case kReduceScatter:    n1 = W * IS; n2 = IS; n3 = 0; break;
+    case kAllReduceOneShot: n1 = IS; n2 = IS; n3 = 0; break;
+    default:                n1 = IS; n2 = 0; n3 = (W - 1) * IS; break;  // all-gather
+  }
+  const int64_t total = n1 + n2 + n3;
+
+  // Quantise one block of the (residual-corrected) input and return its codes.
+  // Elements of shard d that exist in the input.
+  auto shard_lim = [&](int d) -> int64_t {
+    const int64_t rest = p.n - static_cast<int64_t>(d) * p.in_stride;
+    return rest < p.shard_valid ? rest : p.shard_valid;
+  };
+  // Quantise block [base+off, base+off+1024) (valid below base+lim) of the
+  // residual-corrected input; returns its packed words and scale.
+  auto quantize_block = [&](int64_t base, int64_t off, int64_t lim, bool sr, uint32_t stream,
+                            uint32_t (&w)[B], float& scale) {
+    const int64_t elem_base = base + off;
+    const int64_t n_valid = base + lim;
+    const int64_t base_bytes = base * static_cast<int64_t>(sizeof(T));
+    float v[32];
+    load_block<T>(in, elem_base, n_valid, vec_in && (base_bytes & 15) == 0, lane, v);
+    if (p.residual) {
+      float r[32];
+      load_block<float>(p.residual, elem_base, n_valid, vec_res && ((base * 4) & 15) == 0, lane, r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += r[j];
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = warp_max(amax);
+    scale = C::scale_of(amax);
+    uint32_t codes[32];
+    float deq[32];
+    const uint64_t grp0 = static_cast<uint64_t>(elem_base >> 2) + lane;
+    C::encode(v, scale, sr, grp0, stream, p.seed, p.offset, codes, deq);
+    pack32<B>(codes, w);
+    if (p.residual) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) deq[j] = v[j] - deq[j];
+      store_block<float>(p.residual, elem_base, n_valid, vec_res && ((base * 4) & 15) == 0, lane, deq);
+    }
+  };
+
+  while (true) {
+    if (threadIdx.x == 0) {
+      uint32_t it = atomicAdd(p.ticket, 1u);
+      if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) it = 0xffffffffu;
+      s_item = it;
+    }
+    __syncthreads();
+    const int64_t item = s_item;
+    __syncthreads();
+    if (item >= total) break;
+
+    if (item < n1) {
+      // ------------------------------------------------------------ phase 1
+      if (p.op == kAllReduceTwoShot || p.op == kReduceScatter) {
+        const int64_t c = item / W;
+        const int dst = (me + 1 + static_cast<int>(item % W)) % W;
+        const int64_t lim = shard_lim(dst);
+        for (int g = 0; g < p.sub_per_item; ++g) {
+          const int64_t sub = c * p.sub_per_item + g;
+          if (sub >= p.n_sub) break;
+          const int64_t off = sub * kSubElems + warp * kBlockElems;
+          uint32_t w[B];
+          float scale;
+          quantize_block(dst * p.in_stride, off, lim, p.stochastic != 0, 1u + 4u * me, w, scale);
+          uint8_t* dsts = rs_sub(p, dst, me, sub);
+          put_words<B>(dsts, warp, lane, w);
+          if (lane == 0) put_scale(dsts, warp, scale);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) signal(p, rs_flag(p, dst, me, c));
+      } else {
+        // one-shot all-reduce / all-gather: quantise once, store to every rank.
+        const int64_t c = item;
+        for (int g = 0; g < p.sub_per_item; ++g) {
+          const int64_t sub = c * p.sub_per_item + g;
+          if (sub >= p.n_sub) break;
+          const int64_t blk_base = sub * kSubElems + warp * kBlockElems;
+          uint32_t w[B];
+          float scale;
+          quantize_block(0, blk_base, p.n, p.stochastic != 0, 1u + 4u * me, w, scale);
+          for (int k = 0; k < W; ++k) {
+            const int dst = (me + 1 + k) % W;
+            uint8_t* dsts = (p.op == kAllGather) ? ag_sub(p, dst, me, sub) : rs_sub(p, dst, me, sub);
+            put_words<B>(dsts, warp, lane, w);
+            if (lane == 0) put_scale(dsts, warp, scale);
+          }
+          if (p.op == kAllGather) {
+            // own shard of the output = dequantised own codes (identical on every rank)
+            uint32_t codes[32];
+            unpack32<B>(w, codes);
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = C::decode(codes[j], scale) * p.post_scale;
+            store_block<T>(out + me * p.n, blk_base, p.n, vec_ag(me), lane, v);
+          }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          for (int k = 0; k < W; ++k) {
+            const int dst = (me + 1 + k) % W;
+            signal(p, (p.op == kAllGather) ? ag_flag(p, dst, me, c) : rs_flag(p, dst, me, c));
+          }
+        }
+      }
+    } else if (item < n1 + n2) {
+      // ------------------------------------------------------------ phase 2
+      const int64_t c = item - n1;
+      if (threadIdx.x < W) s_flags[threadIdx.x] = rs_flag(p, me, threadIdx.x, c);
+      __syncthreads();
+      if (!cta_wait(p, s_flags, W, &s_ok)) break;
+      for (int g = 0; g < p.sub_per_item; ++g) {
+        const int64_t sub = c * p.sub_per_item + g;
+        if (sub >= p.n_sub) break;
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+        for (int s = 0; s < W; ++s) {
+          const uint8_t* src = rs_sub(p, me, s, sub);
+          uint32_t w[B];
+          get_words<B>(src, warp, lane, w);
+          const float sc = get_scale(src, warp);
+          uint32_t codes[32];
+          unpack32<B>(w, codes);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] += C::decode(codes[j], sc);
+        }
+        if (p.op == kAllReduceTwoShot) {
+          float amax = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(acc[j]));
+          amax = warp_max(amax);
+          const float scale = C::scale_of(amax);
+          uint32_t codes[32];
+          float deq[32];
+          const int64_t elem_base = me * p.shard_len + sub * kSubElems + warp * kBlockElems;
+          C::encode(acc, scale, p.stochastic2 != 0, static_cast<uint64_t>(elem_base >> 2) + lane,
+                    2u + 4u * me, p.seed, p.offset, codes, deq);
+          uint32_t w[B];
+          pack32<B>(codes, w);
+          for (int k = 0; k < W; ++k) {
+            const int dst = (me + 1 + k) % W;
+            uint8_t* d = ag_sub(p, dst, me, sub);
+            put_words<B>(d, warp, lane, w);
+            if (lane == 0) put_scale(d, warp, scale);
+          }
+          // Own output: decode exactly as the other ranks will.
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = C::decode(codes[j], scale) * p.post_scale;
+          store_block<T>(out, elem_base, p.n, vec_out, lane, v);
+        } else if (p.op == kReduceScatter) {
+          const int64_t off = sub * kSubElems + warp * kBlockElems;
+          const int64_t lim = shard_lim(me);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] *= p.post_scale;
+          store_block<T>(out, off, lim, vec_out, lane, acc);
+        } else {  // one-shot
+          const int64_t off = sub * kSubElems + warp * kBlockElems;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] *= p.post_scale;
+          store_block<T>(out, off, p.n, vec_out, lane, acc);
+        }
+      }
+      if (p.op == kAllReduceTwoShot) {
+        __syncthreads();
+        if (threadIdx.x == 0)
+          for (int k = 0; k < W; ++k) {
+            const int dst = (me + 1 + k) % W;
+            signal(p, ag_flag(p, dst, me, c));
+          }
+      }
+    } else {
+      // ------------------------------------------------------------ phase 3
+      const int64_t k3 = item - n1 - n2;
+      const int64_t c = k3 / (W - 1);
+      const int src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
+      if (threadIdx.x == 0) s_flags[0] = ag_flag(p, me, src, c);
+      __syncthreads();
+      if (!cta_wait(p, s_flags, 1, &s_ok)) break;
+      // all-reduce: the source's shard of the full output; all-gather: the
+      // source's slice of the gathered output (n = per-rank shard elements).
+      for (int g = 0; g < p.sub_per_item; ++g) {
+        const int64_t sub = c * p.sub_per_item + g;
+        if (sub >= p.n_sub) break;
+        const uint8_t* srcp = ag_sub(p, me, src, sub);
+        uint32_t w[B];
+        get_words<B>(srcp, warp, lane, w);
+        const float sc = get_scale(srcp, warp);
+        uint32_t codes[32];
+        unpack32<B>(w, codes);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = C::decode(codes[j], sc) * p.post_scale;
+        if (p.op == kAllGather) {
+          store_block<T>(out + src * p.n, sub * kSubElems + warp * kBlockElems, p.n, vec_ag(src),
+                         lane, v);
+        } else {
+          store_block<T>(out, src * p.shard_len + sub * kSubElems + warp * kBlockElems, p.n,
+                         vec_out, lane, v);
+        }
+      }
+    }
+  }
+
+  // Exit bookkeeping: the last CTA out resets the launch-local counters.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.done, 1u);
+    if (prev == gridDim.x - 1) {
+      *p.ticket = 0u;
+      *p.done = 0u;
+      *p.abort_flag = 0u;
+      __threadfence();
+    }
+  }
+}
+
+template <typename F>
+void dispatch_bits_fmt(int bits, int fmt, F&& f) {
+  if (fmt == kFmtE4M3) {
+    if (bits != 8) throw std::runtime_error("bitscom: the E4M3 wire format needs bitwidth 8");
+    f(std::integral_constant<int, 8>{}, std::integral_constant<int, kFmtE4M3>{});
+    return;
+  }
+  switch (bits) {
+    case 1: f(std::integral_constant<int, 1>{}, std::integral_constant<int, kFmtInt>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}, std::integral_constant<int, kFmtInt>{}); break;
+    case 4: f(std::integral_constant<int, 4>{}, std::integral_constant<int, kFmtInt>{}); break;
+    case 8: f(std::integral_constant<int, 8>{}, std::integral_constant<int, kFmtInt>{}); break;
+    case 12: f(std::integral_constant<int, 12>{}, std::integral_constant<int, kFmtInt>{}); break;
+    case 16: f(std::integral_constant<int, 16>{}, std::integral_constant<int, kFmtInt>{}); break;
+    default: throw std::runtime_error("bitscom: bitwidth must be one of 1,2,4,8,12,16");
+  }
+}
+
+}  // namespace
+
+namespace launch {
+
+int64_t coll_sub_bytes(int bits) { return kHeaderBytes + static_cast<int64_t>(kSubBlocks) * 128 * bits; }
+
+void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s) {
+  if (p.world < 1 || p.world > kMaxRanks) throw std::runtime_error("bitscom: world size must be 1..8");
+  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) {
+    constexpr int B = decltype(bc)::value;
+    constexpr int F = decltype(fc)::value;
+    switch (dt) {
+      case kF32: lowbit_coll_kernel<float, B, F><<<grid, kThreads, 0, s>>>(p); break;
+      case kBF16: lowbit_coll_kernel<__nv_bfloat16, B, F><<<grid, kThreads, 0, s>>>(p); break;
+      case kF16: lowbit_coll_kernel<__half, B, F><<<grid, kThreads, 0, s>>>(p); break;
+      default: throw std::runtime_error("bitscom: unsupported dtype");
+    }
+  });
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("lowbit_coll_kernel: ") + cudaGetErrorString(e));
+}
+
+}  // namespace launch
+}  // namespace bitscom

@@ -1,0 +1,305 @@
+// LowBitComm implementation (see comm.h).
+//
+// Workspace layout (bytes, per rank):
+//   [0, 4096)                   local counters (ticket, done, abort, fault-skip)
+//   [flag_off, data_off)        4 flag arrays: rs/ag x parity 0/1, flag_cap words each
+//   [data_off, end)             4 data regions of half_bytes: rs0, ag0, rs1, ag1
+// A data region holds `world` slots; a slot holds `slot_subs` packed
+// sub-chunks of the current bitwidth, so capacity adapts per call.
+// Double-buffering by epoch parity makes back-to-back launches safe without a
+// barrier: finishing launch e on any rank requires every peer's data of launch
+// e, which every peer sends only after finishing launch e-1.
+#include "comm.h"
+
+#include <algorithm>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+namespace bitscom {
+namespace {
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("bitscom LowBitComm: ") + what + ": " + cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) ck(cudaSetDevice(dev), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+constexpr int64_t kCounterBytes = 4096;
+constexpr int64_t kMinSubBytes = kHeaderBytes + kSubBlocks * 128 * 1;  // 1-bit sub-chunk
+constexpr int kTicket = 0, kDone = 32, kAbort = 64, kFaultSkip = 96;  // word indices (128 B apart)
+
+int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
+    : rank_(rank), world_(world), device_(device) {
+  if (world < 1 || world > kMaxRanks) throw std::runtime_error("bitscom: world size must be in 1..8");
+  if (rank < 0 || rank >= world) throw std::runtime_error("bitscom: rank out of range");
+  DeviceGuard g(device_);
+  ck(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device_), "sm count");
+  // Data: 4 regions; flags: 4 arrays sized for the smallest (1-bit) sub-chunk.
+  const int64_t min_ws = 64ll << 20;
+  workspace_bytes = std::max(workspace_bytes, min_ws);
+  half_bytes_ = ((workspace_bytes - kCounterBytes) * 95 / 100 / 4) & ~int64_t(4095);
+  flag_cap_ = half_bytes_ / kMinSubBytes + 1;
+  flag_off_ = kCounterBytes;
+  data_off_ = flag_off_ + ((4 * flag_cap_ * 4 + 4095) & ~int64_t(4095));
+  ws_bytes_ = data_off_ + 4 * half_bytes_;
+  ck(cudaMalloc(&ws_, ws_bytes_), "cudaMalloc(workspace)");
+  ck(cudaMemset(ws_, 0, data_off_), "cudaMemset(flags)");
+  counters_ = reinterpret_cast<uint32_t*>(ws_);
+  ck(cudaHostAlloc(&status_host_, 64, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc(status)");
+  std::memset(status_host_, 0, 64);
+  ck(cudaHostGetDevicePointer(reinterpret_cast<void**>(&status_dev_), status_host_, 0),
+     "cudaHostGetDevicePointer(status)");
+  ck(cudaDeviceSynchronize(), "init sync");
+  peers_[rank_] = ws_;
+  opened_[rank_] = true;
+  if (world_ == 1) ready_ = true;
+  if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) set_timeout_ms(std::atof(t));
+}
+
+LowBitComm::~LowBitComm() {
+  int cur = -1;
+  cudaGetDevice(&cur);
+  cudaSetDevice(device_);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < world_; ++r)
+    if (r != rank_ && opened_[r] && peers_[r]) cudaIpcCloseMemHandle(peers_[r]);
+  if (ws_) cudaFree(ws_);
+  if (status_host_) cudaFreeHost(status_host_);
+  if (cur >= 0) cudaSetDevice(cur);
+}
+
+std::vector<uint8_t> LowBitComm::ipc_handle() const {
+  DeviceGuard g(device_);
+  cudaIpcMemHandle_t h;
+  ck(cudaIpcGetMemHandle(&h, ws_), "cudaIpcGetMemHandle");
+  std::vector<uint8_t> out(sizeof(h));
+  std::memcpy(out.data(), &h, sizeof(h));
+  return out;
+}
+
+void LowBitComm::open_peers(const std::vector<std::vector<uint8_t>>& handles) {
+  if (static_cast<int>(handles.size()) != world_) throw std::runtime_error("bitscom: need one IPC handle per rank");
+  DeviceGuard g(device_);
+  for (int r = 0; r < world_; ++r) {
+    if (r == rank_ || opened_[r]) continue;
+    if (handles[r].size() != sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("bitscom: bad IPC handle size");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles[r].data(), sizeof(h));
+    void* p = nullptr;
+    ck(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    peers_[r] = static_cast<uint8_t*>(p);
+    opened_[r] = true;
+  }
+  ready_ = true;
+}
+
+LowBitComm::Layout LowBitComm::layout(int bits) const {
+  Layout L;
+  L.sub_bytes = launch::coll_sub_bytes(bits);
+  L.slot_subs = half_bytes_ / (world_ * L.sub_bytes);
+  L.slot_items = L.slot_subs;  // at most one flag per sub-chunk
+  if (world_ * L.slot_items > flag_cap_) L.slot_items = flag_cap_ / world_;
+  for (int p = 0; p < 2; ++p) {
+    L.rs_data[p] = data_off_ + (2 * p) * half_bytes_;
+    L.ag_data[p] = data_off_ + (2 * p + 1) * half_bytes_;
+    L.rs_flag[p] = flag_off_ + (2 * p) * flag_cap_ * 4;
+    L.ag_flag[p] = flag_off_ + (2 * p + 1) * flag_cap_ * 4;
+  }
+  return L;
+}
+
+int64_t LowBitComm::max_elems_per_launch(int op, int bits) const {
+  const Layout L = layout(bits);
+  if (op == kAllReduceOneShot) return L.slot_subs * kSubElems;
+  if (op == kAllGather) return L.slot_subs * kSubElems;  // per-rank shard
+  return L.slot_subs * kSubElems * world_;               // full tensor (two-shot / reduce-scatter)
+}
+
+uint32_t LowBitComm::status() const { return *reinterpret_cast<volatile uint32_t*>(status_host_); }
+
+void LowBitComm::ensure_usable() const {
+  if (broken_) throw std::runtime_error("bitscom: communicator is broken by an earlier timeout; re-create it");
+  if (!ready_) throw std::runtime_error("bitscom: peers are not mapped yet (open_peers not called)");
+}
+
+void LowBitComm::check() const {
+  const uint32_t st = status();
+  if (st != kStatusOk) {
+    broken_ = true;
+    throw std::runtime_error(std::string("bitscom: low-bit collective failed: ") +
+                             ((st & kStatusTimeout) ? "a peer did not signal within the timeout" : "aborted") +
+                             " (rank " + std::to_string(rank_) + ", epoch " + std::to_string(epoch_) + ")");
+  }
+  if (broken_) throw std::runtime_error("bitscom: communicator is broken by an earlier timeout; re-create it");
+}
+
+void LowBitComm::set_fault_skip_signal(bool on) {
+  DeviceGuard g(device_);
+  const uint32_t v = on ? 1u : 0u;
+  ck(cudaMemcpy(counters_ + kFaultSkip, &v, 4, cudaMemcpyHostToDevice), "fault skip");
+}
+
+void LowBitComm::launch(int op, const void* in, void* out, float* residual, int64_t n,
+                        int64_t shard_len, int64_t in_stride, int64_t shard_valid, int64_t n_sub, DType dt, int bits, int fmt, bool sr,
+                        bool sr2, uint64_t seed, uint64_t offset, float post_scale, cudaStream_t s,
+                        int max_ctas) {
+  const Layout L = layout(bits);
+  CollParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.op = op;
+  p.fmt = fmt;
+  p.world = world_;
+  p.rank = rank_;
+  p.epoch = ++epoch_;
+  if (p.epoch == 0) p.epoch = ++epoch_;  // 0 is the "never written" flag value
+  p.parity = static_cast<int>(p.epoch & 1u);
+  p.n = n;
+  p.shard_len = shard_len;
+  p.in_stride = in_stride;
+  p.shard_valid = shard_valid;
+  p.n_sub = n_sub;
+  const int grid_cap = std::max(1, max_ctas > 0 ? std::min(max_ctas, sm_count_) : sm_count_);
+  // Items: enough for ~8 per CTA in phase 1, at most 16 sub-chunks each.
+  const int64_t phase1_units = (op == kAllReduceTwoShot || op == kReduceScatter) ? world_ * n_sub : n_sub;
+  int64_t spi = phase1_units / (8 * static_cast<int64_t>(grid_cap));
+  spi = std::max<int64_t>(1, std::min<int64_t>(16, spi));
+  p.sub_per_item = static_cast<int>(spi);
+  p.n_items_slot = div_up(n_sub, spi);
+  if (p.n_items_slot > L.slot_items) throw std::runtime_error("bitscom: flag capacity exceeded");
+  p.in = in;
+  p.out = out;
+  p.residual = residual;
+  p.post_scale = post_scale;
+  p.stochastic = sr ? 1 : 0;
+  p.stochastic2 = sr2 ? 1 : 0;
+  p.seed = seed;
+  p.offset = offset;
+  for (int r = 0; r < world_; ++r) p.peer_base[r] = peers_[r];
+  p.sub_bytes = L.sub_bytes;
+  p.slot_subs = L.slot_subs;
+  p.slot_items = L.slot_items;
+  for (int q = 0; q < 2; ++q) {
+    p.rs_data_off[q] = L.rs_data[q];
+    p.ag_data_off[q] = L.ag_data[q];
+    p.rs_flag_off[q] = L.rs_flag[q];
+    p.ag_flag_off[q] = L.ag_flag[q];
+  }
+  p.ticket = counters_ + kTicket;
+  p.done = counters_ + kDone;
+  p.abort_flag = counters_ + kAbort;
+  p.fault_skip = counters_ + kFaultSkip;
+  p.status = status_dev_;
+  p.timeout_ns = timeout_ns_;
+
+  int64_t n1, n2, n3;
+  const int64_t IS = p.n_items_slot;
+  switch (op) {
+    case kAllReduceTwoShot: n1 = world_ * IS; n2 = IS; n3 = (world_ - 1) * IS; break;
+    case kReduceScatter: n1 = world_ * IS; n2 = IS; n3 = 0; break;
+    case kAllReduceOneShot: n1 = IS; n2 = IS; n3 = 0; break;
+    default: n1 = IS; n2 = 0; n3 = (world_ - 1) * IS; break;
+  }
+  const int64_t total = n1 + n2 + n3;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid_cap, total)));
+  DeviceGuard g(device_);
+  launch::lowbit_coll(p, dt, bits, grid, s);
+  stats_.launches += 1;
+  const int64_t sub_b = L.sub_bytes;
+  if (op == kAllReduceTwoShot) stats_.wire_bytes += 2ull * (world_ - 1) * n_sub * sub_b;
+  else if (op == kReduceScatter) stats_.wire_bytes += static_cast<uint64_t>(world_ - 1) * n_sub * sub_b;
+  else stats_.wire_bytes += static_cast<uint64_t>(world_ - 1) * n_sub * sub_b;
+}
+
+void LowBitComm::allreduce(const void* in, void* out, float* residual, int64_t n, DType dt, int bits,
+                           int fmt, int algo, bool sr, bool sr_requant, uint64_t seed, uint64_t offset,
+                           float post_scale, cudaStream_t s, int max_ctas) {
+  ensure_usable();
+  if (n <= 0) return;
+  const int esz = dt == kF32 ? 4 : 2;
+  stats_.calls += 1;
+  stats_.elements += static_cast<uint64_t>(n);
+  int a = algo;
+  if (a == kAlgoAuto) {
+    // Small messages are latency bound: one launch-wide broadcast beats two
+    // dependent phases.  Threshold from the W=8 crossover of the two variants.
+    const int64_t packed = n * bits / 8;
+    a = (world_ == 1 || packed <= (world_ <= 2 ? (512ll << 10) : (128ll << 10))) ? kAlgoOneShot : kAlgoTwoShot;
+  }
+  const int op = (a == kAlgoOneShot) ? kAllReduceOneShot : kAllReduceTwoShot;
+  const int64_t cap = max_elems_per_launch(op, bits);
+  if (cap <= 0) throw std::runtime_error("bitscom: workspace too small for this bitwidth");
+  const int64_t seg = (op == kAllReduceOneShot) ? cap : cap;  // elements per launch
+  for (int64_t off = 0; off < n; off += seg) {
+    const int64_t m = std::min(seg, n - off);
+    const char* ip = static_cast<const char*>(in) + off * esz;
+    char* op_ = static_cast<char*>(out) + off * esz;
+    float* rp = residual ? residual + off : nullptr;
+    if (op == kAllReduceOneShot) {
+      stats_.oneshot += 1;
+      const int64_t n_sub = div_up(m, kSubElems);
+      launch(op, ip, op_, rp, m, n_sub * kSubElems, 0, m, n_sub, dt, bits, fmt, sr, sr_requant, seed,
+             offset + static_cast<uint64_t>(off), post_scale, s, max_ctas);
+    } else {
+      stats_.twoshot += 1;
+      const int64_t shard = div_up(div_up(m, world_), kSubElems) * kSubElems;
+      const int64_t n_sub = shard / kSubElems;
+      launch(op, ip, op_, rp, m, shard, shard, shard, n_sub, dt, bits, fmt, sr, sr_requant, seed,
+             offset + static_cast<uint64_t>(off), post_scale, s, max_ctas);
+    }
+  }
+}
+
+void LowBitComm::reduce_scatter(const void* in, void* out, float* residual, int64_t shard, DType dt,
+                                int bits, int fmt, bool sr, uint64_t seed, uint64_t offset,
+                                float post_scale, cudaStream_t s, int max_ctas) {
+  ensure_usable();
+  if (shard <= 0) return;
+  stats_.calls += 1;
+  stats_.elements += static_cast<uint64_t>(shard) * world_;
+  const int64_t shard_pad = div_up(shard, kSubElems) * kSubElems;
+  const int64_t cap = max_elems_per_launch(kReduceScatter, bits) / world_;
+  if (shard_pad > cap) {
+    throw std::runtime_error("bitscom: reduce_scatter shard of " + std::to_string(shard) +
+                             " elements exceeds the workspace capacity of " + std::to_string(cap) +
+                             " (raise BITSCOM_WORKSPACE_MB)");
+  }
+  launch(kReduceScatter, in, out, residual, shard * world_, shard_pad, shard, shard, shard_pad / kSubElems,
+         dt, bits, fmt, sr, false, seed, offset, post_scale, s, max_ctas);
+}
+
+void LowBitComm::all_gather(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
+                            int fmt, bool sr, uint64_t seed, uint64_t offset, cudaStream_t s,
+                            int max_ctas) {
+  ensure_usable();
+  if (shard <= 0) return;
+  stats_.calls += 1;
+  stats_.elements += static_cast<uint64_t>(shard) * world_;
+  const int64_t cap = max_elems_per_launch(kAllGather, bits);
+  if (shard > cap) {
+    throw std::runtime_error("bitscom: all_gather shard of " + std::to_string(shard) +
+                             " elements exceeds the workspace capacity of " + std::to_string(cap) +
+                             " (raise BITSCOM_WORKSPACE_MB)");
+  }
+  const int64_t n_sub = div_up(shard, kSubElems);
+  launch(kAllGather, in, out, residual, shard, n_sub * kSubElems, 0, shard, n_sub, dt, bits, fmt, sr, false, seed,
+         offset, 1.0f, s, max_ctas);
+}
+
+}  // namespace bitscom

@@ -1,0 +1,118 @@
+// LowBitComm: the native runtime behind every fused low-bit collective.
+//
+// It owns one symmetric workspace per rank (a cudaMalloc'd buffer whose IPC
+// handle is exchanged with the peers of the group, so every rank can store
+// straight into every other rank's buffer over NVLink/NVSwitch), the per-rank
+// work/exit counters, a host-mapped status word for bounded-wait errors, and
+// the epoch counter that versions every flag.
+//
+// The reference has no transport of its own: every transfer is an NCCL call
+// made through an owned ProcessGroupNCCL (reference
+// cpp/src/process_group_lowbit.cc:67-70, :254-255, :292, :304).
+//
+// Calls on one LowBitComm must be stream-ordered (like an NCCL communicator):
+// every rank issues the same sequence of collectives, each on a stream that
+// orders it after the previous one.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../kernels/coll_params.h"
+#include "../kernels/launchers.h"
+
+namespace bitscom {
+
+enum Algo : int { kAlgoAuto = 0, kAlgoTwoShot = 1, kAlgoOneShot = 2 };
+
+struct CollStats {
+  uint64_t calls = 0;
+  uint64_t launches = 0;
+  uint64_t elements = 0;
+  uint64_t wire_bytes = 0;  // packed bytes this rank stored to peers
+  uint64_t oneshot = 0;
+  uint64_t twoshot = 0;
+};
+
+class LowBitComm {
+ public:
+  LowBitComm(int rank, int world, int device, int64_t workspace_bytes);
+  ~LowBitComm();
+  LowBitComm(const LowBitComm&) = delete;
+  LowBitComm& operator=(const LowBitComm&) = delete;
+
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+  int device() const { return device_; }
+  int64_t workspace_bytes() const { return ws_bytes_; }
+
+  // 64-byte cudaIpcMemHandle of this rank's workspace.
+  std::vector<uint8_t> ipc_handle() const;
+  // Maps every peer's workspace (handles indexed by rank; own entry ignored).
+  void open_peers(const std::vector<std::vector<uint8_t>>& handles);
+  bool ready() const { return ready_; }
+
+  // All-reduce (SUM) of n elements: out = post_scale * sum_r dequant(quant(in_r + residual_r)).
+  // `residual` (fp32, n elements) is updated in place when non-null.
+  void allreduce(const void* in, void* out, float* residual, int64_t n, DType dt, int bits, int fmt,
+                 int algo, bool sr, bool sr_requant, uint64_t seed, uint64_t offset,
+                 float post_scale, cudaStream_t s, int max_ctas);
+  // Reduce-scatter: `in` holds world*shard elements; this rank receives shard `rank` in `out`.
+  void reduce_scatter(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
+                      int fmt, bool sr, uint64_t seed, uint64_t offset, float post_scale,
+                      cudaStream_t s, int max_ctas);
+  // All-gather: `in` holds `shard` elements; `out` receives world*shard elements.
+  void all_gather(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
+                  int fmt, bool sr, uint64_t seed, uint64_t offset, cudaStream_t s, int max_ctas);
+
+  // Host-mapped status of the launches so far (0 = ok).  Only meaningful once
+  // the launches have completed (stream / event synchronised).
+  uint32_t status() const;
+  // Throws std::runtime_error if a launch reported an error; the communicator
+  // then stays broken (every later call throws) until it is re-created.
+  void check() const;
+  bool broken() const { return broken_; }
+
+  void set_timeout_ms(double ms) { timeout_ns_ = static_cast<uint64_t>(ms * 1e6); }
+  double timeout_ms() const { return static_cast<double>(timeout_ns_) / 1e6; }
+  // Test hook: this rank stops storing its completion flags, so waiting peers time out.
+  void set_fault_skip_signal(bool on);
+  uint32_t epoch() const { return epoch_; }
+  const CollStats& stats() const { return stats_; }
+  void reset_stats() { stats_ = CollStats(); }
+
+  // Segment capacity in elements for an op (for tests and planning).
+  int64_t max_elems_per_launch(int op, int bits) const;
+
+ private:
+  struct Layout {
+    int64_t sub_bytes, slot_subs, slot_items;
+    int64_t rs_data[2], ag_data[2], rs_flag[2], ag_flag[2];
+  };
+  Layout layout(int bits) const;
+  void launch(int op, const void* in, void* out, float* residual, int64_t n, int64_t shard_len,
+              int64_t in_stride, int64_t shard_valid, int64_t n_sub, DType dt, int bits, int fmt, bool sr, bool sr2, uint64_t seed,
+              uint64_t offset, float post_scale, cudaStream_t s, int max_ctas);
+  void ensure_usable() const;
+
+  int rank_, world_, device_;
+  int64_t ws_bytes_;
+  uint8_t* ws_ = nullptr;               // own workspace
+  uint8_t* peers_[kMaxRanks] = {};      // mapped peer workspaces (own at [rank_])
+  bool opened_[kMaxRanks] = {};
+  uint32_t* counters_ = nullptr;        // device: ticket, done, abort, fault_skip (each 128 B apart)
+  uint32_t* status_host_ = nullptr;     // pinned host-mapped
+  uint32_t* status_dev_ = nullptr;
+  int64_t data_off_ = 0, flag_off_ = 0, half_bytes_ = 0, flag_cap_ = 0;
+  uint32_t epoch_ = 0;
+  uint64_t timeout_ns_ = 100ull * 1000ull * 1000ull * 1000ull;  // 100 s default
+  int sm_count_ = 148;
+  bool ready_ = false;
+  mutable bool broken_ = false;
+  CollStats stats_;
+};
+
+}  // namespace bitscom

@@ -1,0 +1,149 @@
+"""Fused collective kernels on one GPU (world size 1: every phase runs, the
+peer stores loop back to the own workspace), checked bit-for-bit against the
+CPU model of the block-scaled format, plus the bounded-wait error path."""
+
+import pytest
+import torch
+
+from bitscom_b200.parallel.comm import Communicator
+
+from . import wire_emulator as emu
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def comm():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    return Communicator.create_local(0, workspace_bytes=64 << 20)
+
+
+def _x(n, seed=0, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, generator=g) * 1e-3
+    idx = torch.randint(0, n, (max(1, n // 100),), generator=g)
+    x[idx] = torch.randn(idx.numel(), generator=g) * 1e-1
+    return x.to(dtype)
+
+
+@pytest.mark.parametrize("bits", [1, 2, 4, 8, 12, 16])
+@pytest.mark.parametrize("algo", ["twoshot", "oneshot"])
+@pytest.mark.parametrize("n", [1, 1000, 8192, 50001])
+def test_allreduce_matches_model(comm, bits, algo, n):
+    x = _x(n, seed=bits + n)
+    t = x.cuda()
+    comm.all_reduce(t, bits=bits, algo=algo, post_scale=0.5)
+    torch.cuda.synchronize()
+    comm.check()
+    model = emu.allreduce_two_shot if algo == "twoshot" else emu.allreduce_one_shot
+    exp, _ = model([x], bits, post_scale=0.5)
+    assert torch.equal(t.cpu(), exp)
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("algo", ["twoshot", "oneshot"])
+def test_allreduce_error_feedback(comm, bits, algo):
+    n = 123457
+    x = _x(n, seed=bits)
+    r = torch.randn(n) * 1e-4
+    t, rg = x.cuda(), r.cuda()
+    comm.all_reduce(t, bits=bits, algo=algo, residual=rg)
+    torch.cuda.synchronize()
+    model = emu.allreduce_two_shot if algo == "twoshot" else emu.allreduce_one_shot
+    exp, res = model([x], bits, residuals=[r])
+    assert torch.equal(t.cpu(), exp)
+    assert torch.equal(rg.cpu(), res[0])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_allreduce_low_precision_io(comm, dtype):
+    x = _x(77777, seed=5, dtype=dtype)
+    t = x.cuda()
+    out = torch.empty_like(t)
+    comm.all_reduce(t, out=out, bits=4)
+    torch.cuda.synchronize()
+    exp, _ = emu.allreduce_two_shot([x.float()], 4)
+    assert out.dtype == dtype
+    assert torch.equal(out.cpu(), exp.to(dtype))
+    assert torch.equal(t.cpu(), x)  # input untouched when out is given
+
+
+def test_allreduce_e4m3(comm):
+    x = _x(40000, seed=11)
+    t = x.cuda()
+    comm.all_reduce(t, bits=8, fmt="e4m3")
+    torch.cuda.synchronize()
+    exp, _ = emu.allreduce_two_shot([x], 8, fmt="e4m3")
+    assert torch.equal(t.cpu(), exp)
+    assert (t.cpu() - x).abs().max() <= x.abs().max() / 8  # 3 mantissa bits
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_reduce_scatter_and_all_gather(comm, bits):
+    n = 20000
+    x = _x(n, seed=bits)
+    out = torch.empty(n, device="cuda")
+    comm.reduce_scatter(out, x.cuda(), bits=bits, post_scale=1.0)
+    g = torch.empty(n, device="cuda")
+    comm.all_gather(g, x.cuda(), bits=bits)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), emu.reduce_scatter([x], bits)[0])
+    assert torch.equal(g.cpu(), emu.all_gather([x], bits))
+
+
+def test_segmented_large_message(comm):
+    cap = comm.native.max_elems_per_launch(0, 16)
+    n = cap + 12345
+    x = _x(n, seed=1)
+    t = x.cuda()
+    before = comm.stats()["launches"]
+    comm.all_reduce(t, bits=16, algo="twoshot")
+    torch.cuda.synchronize()
+    assert comm.stats()["launches"] - before == 2
+    exp1, _ = emu.allreduce_two_shot([x[:cap]], 16)
+    exp2, _ = emu.allreduce_two_shot([x[cap:]], 16)
+    assert torch.equal(t.cpu(), torch.cat([exp1, exp2]))
+
+
+def test_stochastic_rounding_reproducible_and_unbiased(comm):
+    x = torch.full((1 << 16,), 0.3)
+    x[::1024] = 1.0  # every block: amax 1 -> 2-bit scale 1
+    a, b, c = x.cuda(), x.cuda(), x.cuda()
+    comm.all_reduce(a, bits=2, algo="oneshot", stochastic_rounding=True, seed=5, offset=1)
+    comm.all_reduce(b, bits=2, algo="oneshot", stochastic_rounding=True, seed=5, offset=1)
+    comm.all_reduce(c, bits=2, algo="oneshot", stochastic_rounding=True, seed=5, offset=2)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b) and not torch.equal(a, c)
+    mask = torch.ones_like(x, dtype=torch.bool)
+    mask[::1024] = False
+    assert abs(float(a.cpu()[mask].mean()) - 0.3) < 0.01
+
+
+def test_back_to_back_launches_many_epochs(comm):
+    x = _x(300000, seed=2)
+    exp, _ = emu.allreduce_two_shot([x], 4)
+    for _ in range(20):
+        t = x.cuda()
+        comm.all_reduce(t, bits=4, algo="twoshot", max_ctas=7)
+    torch.cuda.synchronize()
+    assert torch.equal(t.cpu(), exp)
+
+
+def test_timeout_returns_error_status_without_faulting(cuda):
+    """A wait that nothing will satisfy: this rank drops its own signals, the
+    kernel gives up after the bounded wait and reports through the status word."""
+    c = Communicator.create_local(0, workspace_bytes=64 << 20)
+    c.set_timeout(0.2)
+    c.native.set_fault_skip_signal(True)
+    t = torch.randn(100000, device="cuda")
+    c.all_reduce(t, bits=4, algo="twoshot")
+    torch.cuda.synchronize()
+    assert c.status() != 0
+    with pytest.raises(RuntimeError, match="did not signal"):
+        c.check()
+    with pytest.raises(RuntimeError, match="broken"):
+        c.all_reduce(t, bits=4)
+    # the CUDA context is still healthy
+    y = torch.ones(10, device="cuda") * 2
+    assert float(y.sum()) == 20.0

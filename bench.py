@@ -141,12 +141,18 @@ def build_reference(args, rank, world, local):
     sys.path.insert(0, ref_path)
     import bitscom  # the reference package
     import torchvision
+    from bitscom.api import LowBitGroup
 
-    bitscom.init(bitwidth=args.bits, error_feedback=True)
-    if world > 1:
-        dist.init_process_group("lowbit", timeout=datetime.timedelta(seconds=120))
-    else:
-        dist.init_process_group("lowbit", init_method="tcp://127.0.0.1:%s" % os.environ["MASTER_PORT"], rank=0, world_size=1)
+    # The reference's only error-feedback path is its C++ `lowbit` backend,
+    # whose construction crashed with SIGSEGV on the B200 box (recorded in
+    # DESIGN.md), so this arm runs the reference's documented alternative:
+    # LowBitGroup over an existing NCCL process group (reference api.py
+    # docstring, "way 2"), with the bucketed all-reduce of its own benchmark
+    # (benchmarks/multimodel_stochastic_e2e_curve.py:207-244).  That path has
+    # no error feedback.
+    kw = {} if world > 1 else {"init_method": "tcp://127.0.0.1:%s" % os.environ["MASTER_PORT"], "rank": 0, "world_size": 1}
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), **kw)
+    group = LowBitGroup(bitwidth=args.bits, process_group=dist.group.WORLD)
     torch.manual_seed(0)
     model = torchvision.models.resnet18(num_classes=10)
     model.conv1 = nn.Conv2d(3, 64, 3, 1, 1, bias=False)
@@ -155,47 +161,39 @@ def build_reference(args, rank, world, local):
     for p in model.parameters():  # same initial weights on every rank
         dist.broadcast(p.data, 0)
     opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9)
-    params = [p for p in model.parameters()]
-    # Persistent flat buckets (so the reference's TensorImpl-keyed EF residual
-    # persists across steps), padded to a multiple of world size as its C++
-    # path requires; gradients are all-reduced through dist.all_reduce on the
-    # lowbit process group, the reference's error-feedback path.
     cap = int(args.bucket_mb * 2**20 / 4)
-    buckets, cur, size = [], [], 0
-    for p in reversed(params):
-        if cur and size + p.numel() > cap:
-            buckets.append(cur)
-            cur, size = [], 0
-        cur.append(p)
-        size += p.numel()
-    if cur:
-        buckets.append(cur)
-    flats = []
-    for b in buckets:
-        n = sum(p.numel() for p in b)
-        n += (-n) % world
-        flats.append(torch.zeros(n, device="cuda"))
+
+    def sync_grads(grads):
+        bucket, size = [], 0
+
+        def flush():
+            flat = torch.cat([g.contiguous().view(-1) for g in bucket])
+            group.all_reduce(flat, async_op=False)
+            flat.div_(world)
+            off = 0
+            for g in bucket:
+                g.copy_(flat[off : off + g.numel()].view_as(g))
+                off += g.numel()
+
+        for g in grads:
+            if bucket and size + g.numel() > cap:
+                flush()
+                bucket, size = [], 0
+            bucket.append(g)
+            size += g.numel()
+        if bucket:
+            flush()
 
     def step(x, y):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             loss = F.cross_entropy(model(x), y)
         loss.backward()
-        for b, flat in zip(buckets, flats):
-            off = 0
-            for p in b:
-                flat[off : off + p.numel()].copy_(p.grad.view(-1))
-                off += p.numel()
-            dist.all_reduce(flat).wait()
-            flat.div_(world)
-            off = 0
-            for p in b:
-                p.grad.copy_(flat[off : off + p.numel()].view_as(p.grad))
-                off += p.numel()
+        sync_grads([p.grad for p in model.parameters() if p.grad is not None])
         opt.step()
         opt.zero_grad(set_to_none=False)
         return loss
 
-    return step, (lambda: 0), "reference bitscom lowbit backend (dist.all_reduce, C++ EF path)"
+    return step, (lambda: 0), "reference bitscom LowBitGroup over NCCL, bucketed after backward (no EF path available)"
 
 
 # ----------------------------------------------------------------------------

@@ -16,8 +16,6 @@ each bucket lives in :class:`LowBitHookState` (keyed by bucket index, shape
 checked) and is checkpointable through ``state_dict()``.
 """
 
-from __future__ import annotations
-
 from typing import Dict, Optional
 
 import torch
@@ -128,7 +126,7 @@ def _staged_fallback(state: LowBitHookState, buf: torch.Tensor) -> torch.Tensor:
     return out.div_(state.world_size).to(buf.dtype)
 
 
-def lowbit_allreduce_hook(state: LowBitHookState, bucket) -> torch.futures.Future:
+def lowbit_allreduce_hook(state: LowBitHookState, bucket: dist.GradBucket) -> torch.futures.Future[torch.Tensor]:
     """DDP comm hook: fused low-bit all-reduce (mean) of ``bucket.buffer()``."""
     buf = bucket.buffer()
     world = state.world_size

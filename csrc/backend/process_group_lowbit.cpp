@@ -6,6 +6,8 @@
 #include <ATen/record_function.h>
 #include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <pybind11/chrono.h>
+#include <pybind11/stl.h>
 #include <torch/csrc/distributed/c10d/PrefixStore.hpp>
 #include <torch/extension.h>
 #include <unistd.h>

@@ -138,12 +138,14 @@ struct Codec<B, kFmtInt> {
         float q = sr ? sr_round(x, rr[m]) : rintf(x);
         q = fminf(fmaxf(q, static_cast<float>(qmin)), static_cast<float>(qmax));
         codes[k * 4 + m] = static_cast<uint32_t>(static_cast<int>(q) - qmin);
-        deq[k * 4 + m] = q * scale;
+        // __fmul_rn: never contracted into an FMA with a later add, so the
+        // residual and the reduction see exactly the decoded value.
+        deq[k * 4 + m] = __fmul_rn(q, scale);
       }
     }
   }
   __device__ __forceinline__ static float decode(uint32_t code, float scale) {
-    return static_cast<float>(static_cast<int>(code) + qmin) * scale;
+    return __fmul_rn(static_cast<float>(static_cast<int>(code) + qmin), scale);
   }
 };
 
@@ -169,7 +171,7 @@ struct Codec<B, kFmtE4M3> {
   }
   __device__ __forceinline__ static float decode(uint32_t code, float scale) {
     const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
-    return __half2float(__half(h)) * scale;
+    return __fmul_rn(__half2float(__half(h)), scale);
   }
 };
 
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
       float r[32];
       load_block<float>(p.residual, elem_base, n_valid, vec_res && ((base * 4) & 15) == 0, lane, r);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += r[j];
+      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
     }
     float amax = 0.0f;
 #pragma unroll
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
     pack32<B>(codes, w);
     if (p.residual) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) deq[j] = v[j] - deq[j];
+      for (int j = 0; j < 32; ++j) deq[j] = __fsub_rn(v[j], deq[j]);
       store_block<float>(p.residual, elem_base, n_valid, vec_res && ((base * 4) & 15) == 0, lane, deq);
     }
   };
@@ -403,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
             unpack32<B>(w, codes);
             float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = C::decode(codes[j], scale) * p.post_scale;
+            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(C::decode(codes[j], scale), p.post_scale);
             store_block<T>(out + me * p.n, blk_base, p.n, vec_ag(me), lane, v);
           }
         }
@@ -435,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
           uint32_t codes[32];
           unpack32<B>(w, codes);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] += C::decode(codes[j], sc);
+          for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], C::decode(codes[j], sc));
         }
         if (p.op == kAllReduceTwoShot) {
           float amax = 0.0f;
@@ -459,18 +461,18 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
           // Own output: decode exactly as the other ranks will.
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = C::decode(codes[j], scale) * p.post_scale;
+          for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(C::decode(codes[j], scale), p.post_scale);
           store_block<T>(out, elem_base, p.n, vec_out, lane, v);
         } else if (p.op == kReduceScatter) {
           const int64_t off = sub * kSubElems + warp * kBlockElems;
           const int64_t lim = shard_lim(me);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] *= p.post_scale;
+          for (int j = 0; j < 32; ++j) acc[j] = __fmul_rn(acc[j], p.post_scale);
           store_block<T>(out, off, lim, vec_out, lane, acc);
         } else {  // one-shot
           const int64_t off = sub * kSubElems + warp * kBlockElems;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] *= p.post_scale;
+          for (int j = 0; j < 32; ++j) acc[j] = __fmul_rn(acc[j], p.post_scale);
           store_block<T>(out, off, p.n, vec_out, lane, acc);
         }
       }
@@ -503,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
         unpack32<B>(w, codes);
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = C::decode(codes[j], sc) * p.post_scale;
+        for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(C::decode(codes[j], sc), p.post_scale);
         if (p.op == kAllGather) {
           store_block<T>(out + src * p.n, sub * kSubElems + warp * kBlockElems, p.n, vec_ag(src),
                          lane, v);

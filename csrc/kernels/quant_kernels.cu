@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kThreads)
     if (out) {
       if (q16) __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) sm[lane * kPitch + j] *= sc;
+      for (int j = 0; j < 32; ++j) sm[lane * kPitch + j] = __fmul_rn(sm[lane * kPitch + j], sc);
       __syncwarp();
       store_tile<OutT>(out, base, n, vec_out, sm, lane);
     }
@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(kThreads)
     float q = SR ? sr_round(v, r) : rintf(v);
     q = fminf(fmaxf(q, static_cast<float>(qmin)), static_cast<float>(qmax));
     (void)e;
-    return q * scale;
+    return __fmul_rn(q, scale);  // not contracted with the residual subtraction
   };
   const int64_t n4 = vec ? n / 4 : 0;
   for (int64_t i = tid; i < n4; i += nthr) {
@@ -421,20 +421,20 @@ __global__ void __launch_bounds__(kThreads)
     float o[4], nr[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float c = v[k] + r[k];
+      const float c = __fadd_rn(v[k], r[k]);
       o[k] = one(c, 4 * i + k, pick(rnd, k));
-      nr[k] = c - o[k];
+      nr[k] = __fsub_rn(c, o[k]);
     }
     ElemIO<T>::store4(y + 4 * i, o);
     if (residual) ElemIO<float>::store4(residual + 4 * i, nr);
   }
   for (int64_t i = 4 * n4 + tid; i < n; i += nthr) {
-    const float c = ElemIO<T>::load(x + i) + (residual ? residual[i] : 0.0f);
+    const float c = __fadd_rn(ElemIO<T>::load(x + i), residual ? residual[i] : 0.0f);
     Philox4 rnd{0u, 0u, 0u, 0u};
     if constexpr (SR) rnd = philox_at(static_cast<uint64_t>(i) >> 2, seed, offset);
     const float o = one(c, i, pick(rnd, static_cast<int>(i & 3)));
     ElemIO<T>::store(y + i, o);
-    if (residual) residual[i] = c - o;
+    if (residual) residual[i] = __fsub_rn(c, o);
   }
 }
 

@@ -192,7 +192,9 @@ std::shared_ptr<LowBitComm> ProcessGroupLowBit::comm(int device) {
   // Collective rendezvous over the store: publish host / device / IPC handle,
   // try to map every peer, then agree on the outcome (all or nothing).
   const int W = getSize(), R = getRank();
-  const std::string gen = "bitscom_lowbit/" + std::to_string(device);
+  // Keyed by how many communicators this backend created so far (identical on
+  // every rank), not by the device index (which differs between ranks).
+  const std::string gen = "bitscom_lowbit/" + std::to_string(comm_generation_++);
   std::shared_ptr<LowBitComm> c;
   std::string err;
   try {

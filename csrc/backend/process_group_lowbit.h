@@ -180,6 +180,7 @@ class ProcessGroupLowBit : public c10d::Backend {
   std::unordered_map<int64_t, at::Tensor> residuals_;  // keyed by TensorImpl address (reference parity)
   std::vector<c10::intrusive_ptr<WorkLowBit>> recent_;  // for early error surfacing
   uint64_t sr_calls_ = 0;
+  int comm_generation_ = 0;
   int64_t fused_calls_ = 0, staged_calls_ = 0, forwarded_calls_ = 0;
 };
 

@@ -20,7 +20,10 @@ def _pack(obj):
     import torch
 
     if isinstance(obj, torch.Tensor):
-        return ("__tensor__", obj.detach().cpu().numpy().copy(), str(obj.dtype))
+        t = obj.detach().cpu()
+        if t.dtype in (torch.bfloat16, torch.float16):
+            return ("__tensor__", t.view(torch.int16).numpy().copy(), str(t.dtype))
+        return ("__tensor__", t.numpy().copy(), str(t.dtype))
     if isinstance(obj, (list, tuple)):
         return type(obj)(_pack(o) for o in obj)
     if isinstance(obj, dict):
@@ -32,7 +35,10 @@ def _unpack(obj):
     import torch
 
     if isinstance(obj, tuple) and len(obj) == 3 and obj[0] == "__tensor__":
-        return torch.from_numpy(obj[1])
+        t = torch.from_numpy(obj[1])
+        if obj[2] in ("torch.bfloat16", "torch.float16"):
+            t = t.view(getattr(torch, obj[2].split(".")[1]))
+        return t
     if isinstance(obj, (list, tuple)):
         return type(obj)(_unpack(o) for o in obj)
     if isinstance(obj, dict):

@@ -82,5 +82,9 @@ int64_t coll_sub_bytes(int bits);
 // Launches one fused low-bit collective (see lowbit_coll.cu).
 void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s);
 
+// The same launch reporting errors through the return value instead of
+// exceptions (no host allocation on any path).
+cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s);
+
 }  // namespace launch
 }  // namespace bitscom

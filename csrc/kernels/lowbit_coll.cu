@@ -571,5 +571,23 @@ void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t
   if (e != cudaSuccess) throw std::runtime_error(std::string("lowbit_coll_kernel: ") + cudaGetErrorString(e));
 }
 
+// Same launch without exceptions or host allocations (used by the
+// allocation-free entry point); returns cudaErrorInvalidValue for an
+// unsupported configuration.
+cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s) {
+  if (p.world < 1 || p.world > kMaxRanks || grid < 1) return cudaErrorInvalidValue;
+  if (p.fmt == kFmtE4M3 && bits != 8) return cudaErrorInvalidValue;
+  if (bits != 1 && bits != 2 && bits != 4 && bits != 8 && bits != 12 && bits != 16) return cudaErrorInvalidValue;
+  if (dt != kF32 && dt != kBF16 && dt != kF16) return cudaErrorInvalidValue;
+  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) {
+    constexpr int B = decltype(bc)::value;
+    constexpr int F = decltype(fc)::value;
+    if (dt == kF32) lowbit_coll_kernel<float, B, F><<<grid, kThreads, 0, s>>>(p);
+    else if (dt == kBF16) lowbit_coll_kernel<__nv_bfloat16, B, F><<<grid, kThreads, 0, s>>>(p);
+    else lowbit_coll_kernel<__half, B, F><<<grid, kThreads, 0, s>>>(p);
+  });
+  return cudaGetLastError();
+}
+
 }  // namespace launch
 }  // namespace bitscom

@@ -23,6 +23,7 @@ SOURCES = [
     "csrc/backend/process_group_lowbit.cpp",
     "csrc/kernels/quant_kernels.cu",
     "csrc/kernels/lowbit_coll.cu",
+    "csrc/kernels/noalloc_allreduce.cu",
 ]
 
 NVCC_FLAGS = [

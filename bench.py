@@ -54,6 +54,8 @@ def parse():
     p.add_argument("--bucket-mb", type=float, default=25.0)
     p.add_argument("--max-ctas", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--ref-path", choices=["ef", "python"], default="ef",
+                   help="reference arm: its C++ error-feedback backend path, or its Python LowBitGroup path")
     return p.parse_args()
 
 
@@ -141,18 +143,25 @@ def build_reference(args, rank, world, local):
     sys.path.insert(0, ref_path)
     import bitscom  # the reference package
     import torchvision
-    from bitscom.api import LowBitGroup
 
-    # The reference's only error-feedback path is its C++ `lowbit` backend,
-    # whose construction crashed with SIGSEGV on the B200 box (recorded in
-    # DESIGN.md), so this arm runs the reference's documented alternative:
-    # LowBitGroup over an existing NCCL process group (reference api.py
-    # docstring, "way 2"), with the bucketed all-reduce of its own benchmark
-    # (benchmarks/multimodel_stochastic_e2e_curve.py:207-244).  That path has
-    # no error feedback.
     kw = {} if world > 1 else {"init_method": "tcp://127.0.0.1:%s" % os.environ["MASTER_PORT"], "rank": 0, "world_size": 1}
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), **kw)
-    group = LowBitGroup(bitwidth=args.bits, process_group=dist.group.WORLD)
+    if args.ref_path == "ef":
+        # The reference's error-feedback path: its C++ `lowbit` backend with
+        # error_feedback=True, reached through dist.all_reduce (reference
+        # README; cpp/src/process_group_lowbit.cc:153-328).  DDP cannot drive
+        # it (its Work future completes before the second phase), so
+        # gradients go through persistent flat buckets — persistent so the
+        # residual, keyed by tensor identity, carries across steps — padded to
+        # a multiple of the world size as that path requires.
+        bitscom.init(bitwidth=args.bits, error_feedback=True)
+        dist.init_process_group("lowbit", timeout=datetime.timedelta(seconds=120), **kw)
+        group = None
+    else:
+        # The reference's Python path: LowBitGroup over an NCCL group (no EF).
+        from bitscom.api import LowBitGroup
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), **kw)
+        group = LowBitGroup(bitwidth=args.bits, process_group=dist.group.WORLD)
     torch.manual_seed(0)
     model = torchvision.models.resnet18(num_classes=10)
     model.conv1 = nn.Conv2d(3, 64, 3, 1, 1, bias=False)
@@ -162,38 +171,49 @@ def build_reference(args, rank, world, local):
         dist.broadcast(p.data, 0)
     opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9)
     cap = int(args.bucket_mb * 2**20 / 4)
+    params = [p for p in model.parameters()]
+    buckets, cur, size = [], [], 0
+    for p in reversed(params):  # gradient-ready order, as DDP buckets them
+        if cur and size + p.numel() > cap:
+            buckets.append(cur)
+            cur, size = [], 0
+        cur.append(p)
+        size += p.numel()
+    if cur:
+        buckets.append(cur)
+    flats = []
+    for b in buckets:
+        n = sum(p.numel() for p in b)
+        flats.append(torch.zeros(n + (-n) % world, device="cuda"))
 
-    def sync_grads(grads):
-        bucket, size = [], 0
-
-        def flush():
-            flat = torch.cat([g.contiguous().view(-1) for g in bucket])
-            group.all_reduce(flat, async_op=False)
+    def sync_grads():
+        for b, flat in zip(buckets, flats):
+            off = 0
+            for p in b:
+                flat[off : off + p.numel()].copy_(p.grad.view(-1))
+                off += p.numel()
+            if group is None:
+                dist.all_reduce(flat).wait()
+            else:
+                group.all_reduce(flat, async_op=False)
             flat.div_(world)
             off = 0
-            for g in bucket:
-                g.copy_(flat[off : off + g.numel()].view_as(g))
-                off += g.numel()
-
-        for g in grads:
-            if bucket and size + g.numel() > cap:
-                flush()
-                bucket, size = [], 0
-            bucket.append(g)
-            size += g.numel()
-        if bucket:
-            flush()
+            for p in b:
+                p.grad.copy_(flat[off : off + p.numel()].view_as(p.grad))
+                off += p.numel()
 
     def step(x, y):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             loss = F.cross_entropy(model(x), y)
         loss.backward()
-        sync_grads([p.grad for p in model.parameters() if p.grad is not None])
+        sync_grads()
         opt.step()
         opt.zero_grad(set_to_none=False)
         return loss
 
-    return step, (lambda: 0), "reference bitscom LowBitGroup over NCCL, bucketed after backward (no EF path available)"
+    desc = ("reference bitscom lowbit backend, error feedback, dist.all_reduce per persistent bucket after backward"
+            if group is None else "reference bitscom LowBitGroup over NCCL, bucketed after backward (no EF)")
+    return step, (lambda: 0), desc
 
 
 # ----------------------------------------------------------------------------

@@ -68,7 +68,7 @@ def main():
     p.add_argument("--max-mb", type=float, default=256)
     p.add_argument("--bits", type=int, nargs="+", default=[4])
     p.add_argument("--fp8", action="store_true", help="also run the E4M3 8-bit format")
-    p.add_argument("--impls", nargs="+", default=["ours", "nccl"], choices=["ours", "nccl", "reference"])
+    p.add_argument("--impls", nargs="+", default=["ours", "nccl"], choices=["ours", "nccl", "reference", "reference_ef"])
     p.add_argument("--no-ef", action="store_true")
     p.add_argument("--no-sr", action="store_true")
     p.add_argument("--algo", default="auto")
@@ -90,9 +90,16 @@ def main():
 
     comm = Communicator.for_group(None, local) if world > 1 else Communicator.create_local(local)
     ref_group = None
-    if "reference" in args.impls:
+    ref_pg = None
+    if "reference" in args.impls or "reference_ef" in args.impls:
         sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
-        from bitscom.api import LowBitGroup as RefGroup  # the reference package
+        import bitscom as ref_bitscom  # the reference package
+        from bitscom.api import LowBitGroup as RefGroup
+    if "reference_ef" in args.impls:
+        # The reference's error-feedback path: its C++ lowbit backend (one
+        # bitwidth per process), reached through dist.all_reduce.
+        ref_bitscom.init(bitwidth=args.bits[0], error_feedback=not args.no_ef)
+        ref_pg = dist.new_group(backend="lowbit")
 
     sizes = []
     s = int(args.min_kb * 1024)
@@ -118,6 +125,10 @@ def main():
                         comm.all_reduce(buf, bits=bits, fmt=fmt, residual=res,
                                         stochastic_rounding=not args.no_sr and fmt == "int",
                                         offset=counter[0], algo=args.algo, max_ctas=args.max_ctas)
+                elif impl == "reference_ef":
+                    if fmt != "int" or bits != args.bits[0] or n % world:
+                        continue
+                    fn = lambda: dist.all_reduce(buf, group=ref_pg)
                 else:
                     if fmt != "int":
                         continue

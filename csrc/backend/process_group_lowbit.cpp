@@ -112,10 +112,12 @@ void WorkLowBit::synchronize() {
 bool WorkLowBit::wait(std::chrono::milliseconds timeout) {
   if (!cuda_) return true;
   synchronize();
-  if (blocking_wait_ || timeout != c10d::kUnsetTimeout) {
+  // kNoTimeout (0) and kUnsetTimeout (-1) both mean "no host-side limit".
+  const bool bounded = timeout.count() > 0;
+  if (blocking_wait_ || bounded) {
     const auto t0 = std::chrono::steady_clock::now();
     while (!event_->query()) {
-      if (timeout != c10d::kUnsetTimeout && std::chrono::steady_clock::now() - t0 > timeout)
+      if (bounded && std::chrono::steady_clock::now() - t0 > timeout)
         TORCH_CHECK(false, "bitscom: Work.wait timed out after ", timeout.count(), " ms");
       std::this_thread::yield();
     }

@@ -8,6 +8,10 @@
 //   * the `lowbit` c10d backend (registered from backend/process_group_lowbit.cpp).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <execinfo.h>
+#include <unistd.h>
+
+#include <csignal>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
@@ -17,6 +21,23 @@
 
 namespace bitscom {
 namespace {
+
+// Debug aid: on SIGSEGV/SIGABRT print the native call stack (glibc
+// backtrace) to stderr, then re-raise with the default action.
+void crash_handler(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char msg[] = "\n[bitscom] native backtrace:\n";
+  (void)!write(2, msg, sizeof(msg) - 1);
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+
+void install_crash_backtrace() {
+  signal(SIGSEGV, crash_handler);
+  signal(SIGABRT, crash_handler);
+}
 
 DType to_dt(at::ScalarType t) {
   switch (t) {
@@ -228,6 +249,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_dtype") = at::kFloat);
   m.def("ef_roundtrip", &ef_roundtrip_op, py::arg("x"), py::arg("residual") = py::none(), py::arg("bits") = 4,
         py::arg("stochastic") = false, py::arg("seed") = 0, py::arg("offset") = 0);
+  m.def("install_crash_backtrace", &install_crash_backtrace,
+        "print the native stack on SIGSEGV/SIGABRT (debugging aid)");
   m.def("packed_bytes", [](int64_t n, int64_t bits) -> int64_t { return packed_bytes_ref(n, static_cast<int>(bits)); });
   m.def("wire_sub_bytes", [](int64_t bits) -> int64_t { return launch::coll_sub_bytes(static_cast<int>(bits)); });
 

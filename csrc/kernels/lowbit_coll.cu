@@ -99,83 +99,6 @@ __device__ __forceinline__ void store_block(T* __restrict__ p, int64_t blk_base,
 }
 
 // ---------------------------------------------------------------------------
-// Codecs.  encode(): 32 values + block scale -> 32 codes; decode(): inverse.
-// ---------------------------------------------------------------------------
-template <int B, int FMT>
-struct Codec;
-
-template <int B>
-struct Codec<B, kFmtInt> {
-  static constexpr int qmin = QBounds<B>::qmin;
-  static constexpr int qmax = QBounds<B>::qmax;
-  __device__ __forceinline__ static float scale_of(float amax) {
-    return amax > 0.0f ? amax / static_cast<float>(qmax) : 1.0f;
-  }
-  // Returns the dequantised value of each code in `deq`.
-  // SR draws come from Philox(counter = {element/4 ^ stream<<52, offset}, key = seed);
-  // stream = phase + 4*rank keeps ranks and phases independent.
-  __device__ __forceinline__ static void encode(const float (&v)[32], float scale, bool sr,
-                                                uint64_t grp0, uint32_t stream, uint64_t seed,
-                                                uint64_t offset, uint32_t (&codes)[32],
-                                                float (&deq)[32]) {
-    const float inv = 1.0f / scale;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      Philox4 r{0u, 0u, 0u, 0u};
-      if (sr) {
-        Philox4 c;
-        const uint64_t g = grp0 + k * 32;
-        c.x = static_cast<uint32_t>(g);
-        c.y = static_cast<uint32_t>(g >> 32) ^ (stream << 20);
-        c.z = static_cast<uint32_t>(offset);
-        c.w = static_cast<uint32_t>(offset >> 32);
-        r = philox4x32_10(c, static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
-      }
-      const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float x = v[k * 4 + m] * inv;
-        float q = sr ? sr_round(x, rr[m]) : rintf(x);
-        q = fminf(fmaxf(q, static_cast<float>(qmin)), static_cast<float>(qmax));
-        codes[k * 4 + m] = static_cast<uint32_t>(static_cast<int>(q) - qmin);
-        // __fmul_rn: never contracted into an FMA with a later add, so the
-        // residual and the reduction see exactly the decoded value.
-        deq[k * 4 + m] = __fmul_rn(q, scale);
-      }
-    }
-  }
-  __device__ __forceinline__ static float decode(uint32_t code, float scale) {
-    return __fmul_rn(static_cast<float>(static_cast<int>(code) + qmin), scale);
-  }
-};
-
-template <int B>
-struct Codec<B, kFmtE4M3> {
-  static_assert(B == 8, "E4M3 codes are 8 bits");
-  __device__ __forceinline__ static float scale_of(float amax) {
-    return amax > 0.0f ? amax / 448.0f : 1.0f;
-  }
-  __device__ __forceinline__ static void encode(const float (&v)[32], float scale, bool,
-                                                uint64_t, uint32_t, uint64_t, uint64_t,
-                                                uint32_t (&codes)[32], float (&deq)[32]) {
-    const float inv = 1.0f / scale;
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-      const float2 f = make_float2(v[j] * inv, v[j + 1] * inv);
-      const __nv_fp8x2_storage_t c2 = __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
-      codes[j] = c2 & 0xffu;
-      codes[j + 1] = (c2 >> 8) & 0xffu;
-      deq[j] = decode(codes[j], scale);
-      deq[j + 1] = decode(codes[j + 1], scale);
-    }
-  }
-  __device__ __forceinline__ static float decode(uint32_t code, float scale) {
-    const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
-    return __fmul_rn(__half2float(__half(h)), scale);
-  }
-};
-
-// ---------------------------------------------------------------------------
 // Packed sub-chunk I/O.  Lane-interleaved payload: vector r of lane l sits at
 // vector index r*32 + l.
 // ---------------------------------------------------------------------------
@@ -265,29 +188,131 @@ __device__ __forceinline__ void signal(const CollParams& p, uint32_t* flag) {
   st_release_sys(flag, p.epoch);
 }
 
-// Thread 0 waits on every flag in flags[0..count) (stride `stride` words);
-// the verdict is broadcast to the CTA.
-__device__ bool cta_wait(const CollParams& p, uint32_t* const* flags, int count, bool* ok_smem) {
-  if (threadIdx.x == 0) {
-    bool ok = true;
-    for (int i = 0; i < count && ok; ++i) ok = wait_epoch(p, flags[i]);
-    *ok_smem = ok;
+// ---------------------------------------------------------------------------
+// Codes <-> words, one element at a time (j is a compile-time constant inside
+// the unrolled loops, so every shift and word index folds away).
+// ---------------------------------------------------------------------------
+template <int B>
+__device__ __forceinline__ void put_code(uint32_t (&w)[B], int j, uint32_t code) {
+  const int bit = j * B, wi = bit >> 5, off = bit & 31;
+  w[wi] |= code << off;
+  if (off + B > 32) w[wi + 1] |= code >> (32 - off);
+}
+
+template <int B>
+__device__ __forceinline__ uint32_t get_code(const uint32_t (&w)[B], int j) {
+  const int bit = j * B, wi = bit >> 5, off = bit & 31;
+  uint32_t x = w[wi] >> off;
+  if (off + B > 32) x |= w[wi + 1] << (32 - off);
+  return x & QBounds<B>::mask;
+}
+
+// ---------------------------------------------------------------------------
+// Codecs: block scale, per-element encode (value -> code, dequantised value)
+// and decode.  Products use __fmul_rn so no FMA contraction can change a
+// decoded value between the encoder, the reducer and the decoders.
+// ---------------------------------------------------------------------------
+template <int B, int FMT>
+struct Codec;
+
+template <int B>
+struct Codec<B, kFmtInt> {
+  static constexpr int qmin = QBounds<B>::qmin;
+  static constexpr int qmax = QBounds<B>::qmax;
+  __device__ __forceinline__ static float scale_of(float amax) {
+    return amax > 0.0f ? amax / static_cast<float>(qmax) : 1.0f;
   }
-  __syncthreads();
-  const bool ok = *ok_smem;
-  __syncthreads();
-  return ok;
+  // x = value * (1/scale); r = random bits (used when sr).
+  __device__ __forceinline__ static uint32_t encode(float x, bool sr, uint32_t r, float scale, float& deq) {
+    float q = sr ? sr_round(x, r) : rintf(x);
+    q = fminf(fmaxf(q, static_cast<float>(qmin)), static_cast<float>(qmax));
+    deq = __fmul_rn(q, scale);
+    return static_cast<uint32_t>(static_cast<int>(q) - qmin);
+  }
+  __device__ __forceinline__ static float decode(uint32_t code, float scale) {
+    return __fmul_rn(static_cast<float>(static_cast<int>(code) + qmin), scale);
+  }
+};
+
+template <int B>
+struct Codec<B, kFmtE4M3> {
+  static_assert(B == 8, "E4M3 codes are 8 bits");
+  __device__ __forceinline__ static float scale_of(float amax) {
+    return amax > 0.0f ? amax / 448.0f : 1.0f;
+  }
+  __device__ __forceinline__ static uint32_t encode(float x, bool, uint32_t, float scale, float& deq) {
+    const __nv_fp8_storage_t c = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+    deq = decode(c, scale);
+    return c;
+  }
+  __device__ __forceinline__ static float decode(uint32_t code, float scale) {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
+    return __fmul_rn(__half2float(__half(h)), scale);
+  }
+};
+
+// Philox draws of the float4 group `grp` (counter {grp, stream, offset}).
+__device__ __forceinline__ Philox4 sr_draws(uint64_t grp, uint32_t stream, uint64_t seed, uint64_t offset) {
+  Philox4 c;
+  c.x = static_cast<uint32_t>(grp);
+  c.y = static_cast<uint32_t>(grp >> 32) ^ (stream << 20);
+  c.z = static_cast<uint32_t>(offset);
+  c.w = static_cast<uint32_t>(offset >> 32);
+  return philox4x32_10(c, static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
+}
+
+__device__ __forceinline__ uint32_t lane_of(const Philox4& r, int m) {
+  return m == 0 ? r.x : (m == 1 ? r.y : (m == 2 ? r.z : r.w));
+}
+
+// What encode_block leaves in v.
+enum EncodeKeep : int { kKeepInput = 0, kKeepResidual = 1, kKeepDequant = 2 };
+
+// Quantises the 32 values of this lane with the warp-wide block scale:
+// packs the codes into w, returns the scale, and replaces v[j] with
+// (v[j] - dequantised), the new error-feedback residual (kKeepResidual), or
+// with the dequantised value itself (kKeepDequant, bit-identical to decoding
+// the packed code).
+template <int B, int FMT, int KEEP>
+__device__ __forceinline__ float encode_block(float (&v)[32], bool sr, uint64_t grp0, uint32_t stream,
+                                              uint64_t seed, uint64_t offset, uint32_t (&w)[B]) {
+  using C = Codec<B, FMT>;
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  amax = warp_max(amax);
+  const float scale = C::scale_of(amax);
+  const float inv = 1.0f / scale;
+#pragma unroll
+  for (int i = 0; i < B; ++i) w[i] = 0u;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    Philox4 r{0u, 0u, 0u, 0u};
+    if (FMT == kFmtInt && sr) r = sr_draws(grp0 + k * 32, stream, seed, offset);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int j = k * 4 + m;
+      float deq;
+      const uint32_t code = C::encode(__fmul_rn(v[j], inv), sr, lane_of(r, m), scale, deq);
+      put_code<B>(w, j, code);
+      if (KEEP == kKeepResidual) v[j] = __fsub_rn(v[j], deq);
+      if (KEEP == kKeepDequant) v[j] = deq;
+    }
+  }
+  return scale;
 }
 
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
 template <typename T, int B, int FMT>
-__global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_constant__ CollParams p) {
+__global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_constant__ CollParams p) {
   using C = Codec<B, FMT>;
-  __shared__ uint32_t s_item;
-  __shared__ bool s_ok;
-  __shared__ uint32_t* s_flags[kMaxRanks];
+  // Double-buffered by item parity: thread 0 writes the next slot while the
+  // CTA still reads the current one; every item has at least one CTA barrier
+  // after that write, which publishes it.
+  __shared__ int64_t s_item[2];
+  __shared__ int s_ok[2];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -297,15 +322,11 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
   const bool vec_in = (reinterpret_cast<uintptr_t>(p.in) & 15u) == 0;
   const bool vec_out = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
   const bool vec_res = (reinterpret_cast<uintptr_t>(p.residual) & 15u) == 0;
+  const bool has_res = p.residual != nullptr;
   const T* in = static_cast<const T*>(p.in);
   T* out = static_cast<T*>(p.out);
-  // All-gather output slices start at src * n elements: vector stores only
-  // when that offset keeps 16-byte alignment.
-  auto vec_ag = [&](int src) {
-    return vec_out && ((static_cast<int64_t>(src) * p.n * static_cast<int64_t>(sizeof(T))) & 15) == 0;
-  };
+  const bool skip_signals = p.fault_skip != nullptr && *p.fault_skip != 0u;  // test hook
 
-  // Phase sizes.
   int64_t n1, n2, n3;
   switch (p.op) {
     case kAllReduceTwoShot: n1 = W * IS; n2 = IS; n3 = (W - 1) * IS; break;
@@ -314,115 +335,97 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
     default:                n1 = IS; n2 = 0; n3 = (W - 1) * IS; break;  // all-gather
   }
   const int64_t total = n1 + n2 + n3;
+  const bool bcast1 = (p.op == kAllReduceOneShot || p.op == kAllGather);  // phase 1 stores to every rank
 
-  // Quantise one block of the (residual-corrected) input and return its codes.
-  // Elements of shard d that exist in the input.
+  // Elements of input shard d that exist.
   auto shard_lim = [&](int d) -> int64_t {
     const int64_t rest = p.n - static_cast<int64_t>(d) * p.in_stride;
     return rest < p.shard_valid ? rest : p.shard_valid;
   };
-  // Quantise block [base+off, base+off+1024) (valid below base+lim) of the
-  // residual-corrected input; returns its packed words and scale.
-  auto quantize_block = [&](int64_t base, int64_t off, int64_t lim, bool sr, uint32_t stream,
-                            uint32_t (&w)[B], float& scale) {
-    const int64_t elem_base = base + off;
-    const int64_t n_valid = base + lim;
-    const int64_t base_bytes = base * static_cast<int64_t>(sizeof(T));
-    float v[32];
-    load_block<T>(in, elem_base, n_valid, vec_in && (base_bytes & 15) == 0, lane, v);
-    if (p.residual) {
-      float r[32];
-      load_block<float>(p.residual, elem_base, n_valid, vec_res && ((base * 4) & 15) == 0, lane, r);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
-    }
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-    amax = warp_max(amax);
-    scale = C::scale_of(amax);
-    uint32_t codes[32];
-    float deq[32];
-    const uint64_t grp0 = static_cast<uint64_t>(elem_base >> 2) + lane;
-    C::encode(v, scale, sr, grp0, stream, p.seed, p.offset, codes, deq);
-    pack32<B>(codes, w);
-    if (p.residual) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) deq[j] = __fsub_rn(v[j], deq[j]);
-      store_block<float>(p.residual, elem_base, n_valid, vec_res && ((base * 4) & 15) == 0, lane, deq);
-    }
+  auto grab = [&]() -> int64_t {
+    const uint32_t t = atomicAdd(p.ticket, 1u);
+    return (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) ? total : static_cast<int64_t>(t);
   };
 
+  if (threadIdx.x == 0) s_item[0] = grab();
+  __syncthreads();
+  int cur = 0;
   while (true) {
-    if (threadIdx.x == 0) {
-      uint32_t it = atomicAdd(p.ticket, 1u);
-      if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) it = 0xffffffffu;
-      s_item = it;
-    }
-    __syncthreads();
-    const int64_t item = s_item;
-    __syncthreads();
+    const int64_t item = s_item[cur];
     if (item >= total) break;
+    // Prefetch the next ticket; its latency hides behind this item's work.
+    if (threadIdx.x == 0) s_item[cur ^ 1] = grab();
 
     if (item < n1) {
       // ------------------------------------------------------------ phase 1
-      if (p.op == kAllReduceTwoShot || p.op == kReduceScatter) {
-        const int64_t c = item / W;
-        const int dst = (me + 1 + static_cast<int>(item % W)) % W;
-        const int64_t lim = shard_lim(dst);
-        for (int g = 0; g < p.sub_per_item; ++g) {
-          const int64_t sub = c * p.sub_per_item + g;
-          if (sub >= p.n_sub) break;
-          const int64_t off = sub * kSubElems + warp * kBlockElems;
-          uint32_t w[B];
-          float scale;
-          quantize_block(dst * p.in_stride, off, lim, p.stochastic != 0, 1u + 4u * me, w, scale);
-          uint8_t* dsts = rs_sub(p, dst, me, sub);
-          put_words<B>(dsts, warp, lane, w);
-          if (lane == 0) put_scale(dsts, warp, scale);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) signal(p, rs_flag(p, dst, me, c));
-      } else {
-        // one-shot all-reduce / all-gather: quantise once, store to every rank.
-        const int64_t c = item;
-        for (int g = 0; g < p.sub_per_item; ++g) {
-          const int64_t sub = c * p.sub_per_item + g;
-          if (sub >= p.n_sub) break;
-          const int64_t blk_base = sub * kSubElems + warp * kBlockElems;
-          uint32_t w[B];
-          float scale;
-          quantize_block(0, blk_base, p.n, p.stochastic != 0, 1u + 4u * me, w, scale);
-          for (int k = 0; k < W; ++k) {
-            const int dst = (me + 1 + k) % W;
-            uint8_t* dsts = (p.op == kAllGather) ? ag_sub(p, dst, me, sub) : rs_sub(p, dst, me, sub);
-            put_words<B>(dsts, warp, lane, w);
-            if (lane == 0) put_scale(dsts, warp, scale);
-          }
-          if (p.op == kAllGather) {
-            // own shard of the output = dequantised own codes (identical on every rank)
-            uint32_t codes[32];
-            unpack32<B>(w, codes);
-            float v[32];
+      const int64_t c = bcast1 ? item : item / W;
+      const int dst = bcast1 ? me : (me + 1 + static_cast<int>(item % W)) % W;
+      const int64_t base = bcast1 ? 0 : static_cast<int64_t>(dst) * p.in_stride;
+      const int64_t lim = bcast1 ? p.n : shard_lim(dst);
+      const bool vx = vec_in && ((base * static_cast<int64_t>(sizeof(T))) & 15) == 0;
+      const bool vr = vec_res && ((base * 4) & 15) == 0;
+      for (int g = 0; g < p.sub_per_item; ++g) {
+        const int64_t sub = c * p.sub_per_item + g;
+        if (sub >= p.n_sub) break;
+        const int64_t off = sub * kSubElems + warp * kBlockElems;
+        float v[32];
+        load_block<T>(in, base + off, base + lim, vx, lane, v);
+        if (has_res) {
+          float r[32];
+          load_block<float>(p.residual, base + off, base + lim, vr, lane, r);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(C::decode(codes[j], scale), p.post_scale);
-            store_block<T>(out + me * p.n, blk_base, p.n, vec_ag(me), lane, v);
+          for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
+        }
+        uint32_t w[B];
+        float scale;
+        if (has_res) {
+          scale = encode_block<B, FMT, kKeepResidual>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
+                                                      1u + 4u * me, p.seed, p.offset, w);
+          store_block<float>(p.residual, base + off, base + lim, vr, lane, v);
+        } else {
+          scale = encode_block<B, FMT, kKeepInput>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
+                                                   1u + 4u * me, p.seed, p.offset, w);
+        }
+        if (!bcast1) {
+          uint8_t* d = rs_sub(p, dst, me, sub);
+          put_words<B>(d, warp, lane, w);
+          if (lane == 0) put_scale(d, warp, scale);
+        } else {
+          for (int k = 0; k < W; ++k) {
+            const int d = (me + 1 + k) % W;
+            uint8_t* dp = (p.op == kAllGather) ? ag_sub(p, d, me, sub) : rs_sub(p, d, me, sub);
+            put_words<B>(dp, warp, lane, w);
+            if (lane == 0) put_scale(dp, warp, scale);
+          }
+          if (p.op == kAllGather) {  // own slice = decoded own codes (identical on every rank)
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = C::decode(get_code<B>(w, j), scale);
+            const bool va = vec_out && ((static_cast<int64_t>(me) * p.n * static_cast<int64_t>(sizeof(T))) & 15) == 0;
+            store_block<T>(out + static_cast<int64_t>(me) * p.n, off, p.n, va, lane, o);
           }
         }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-          for (int k = 0; k < W; ++k) {
-            const int dst = (me + 1 + k) % W;
-            signal(p, (p.op == kAllGather) ? ag_flag(p, dst, me, c) : rs_flag(p, dst, me, c));
-          }
+      }
+      __syncthreads();
+      // Completion flags, released by the last warp while the others move on.
+      if (warp == kThreads / 32 - 1 && !skip_signals) {
+        if (!bcast1) {
+          if (lane == 0) st_release_sys(rs_flag(p, dst, me, c), p.epoch);
+        } else if (lane < W) {
+          const int d = (me + 1 + lane) % W;
+          st_release_sys((p.op == kAllGather) ? ag_flag(p, d, me, c) : rs_flag(p, d, me, c), p.epoch);
         }
       }
     } else if (item < n1 + n2) {
       // ------------------------------------------------------------ phase 2
       const int64_t c = item - n1;
-      if (threadIdx.x < W) s_flags[threadIdx.x] = rs_flag(p, me, threadIdx.x, c);
+      if (threadIdx.x == 0) {
+        bool ok = true;
+        for (int s = 0; s < W && ok; ++s) ok = wait_epoch(p, rs_flag(p, me, s, c));
+        s_ok[cur] = ok ? 1 : 0;
+      }
       __syncthreads();
-      if (!cta_wait(p, s_flags, W, &s_ok)) break;
+      if (!s_ok[cur]) break;
       for (int g = 0; g < p.sub_per_item; ++g) {
         const int64_t sub = c * p.sub_per_item + g;
         if (sub >= p.n_sub) break;
@@ -434,87 +437,67 @@ __global__ void __launch_bounds__(kThreads, 1) lowbit_coll_kernel(const __grid_c
           uint32_t w[B];
           get_words<B>(src, warp, lane, w);
           const float sc = get_scale(src, warp);
-          uint32_t codes[32];
-          unpack32<B>(w, codes);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], C::decode(codes[j], sc));
+          for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], C::decode(get_code<B>(w, j), sc));
         }
+        const int64_t off = sub * kSubElems + warp * kBlockElems;
         if (p.op == kAllReduceTwoShot) {
-          float amax = 0.0f;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(acc[j]));
-          amax = warp_max(amax);
-          const float scale = C::scale_of(amax);
-          uint32_t codes[32];
-          float deq[32];
-          const int64_t elem_base = me * p.shard_len + sub * kSubElems + warp * kBlockElems;
-          C::encode(acc, scale, p.stochastic2 != 0, static_cast<uint64_t>(elem_base >> 2) + lane,
-                    2u + 4u * me, p.seed, p.offset, codes, deq);
+          const int64_t elem_base = static_cast<int64_t>(me) * p.shard_len + off;
           uint32_t w[B];
-          pack32<B>(codes, w);
+          const float scale = encode_block<B, FMT, kKeepDequant>(acc, p.stochastic2 != 0,
+                                                                 static_cast<uint64_t>(elem_base >> 2) + lane,
+                                                                 2u + 4u * me, p.seed, p.offset, w);
           for (int k = 0; k < W; ++k) {
-            const int dst = (me + 1 + k) % W;
-            uint8_t* d = ag_sub(p, dst, me, sub);
-            put_words<B>(d, warp, lane, w);
-            if (lane == 0) put_scale(d, warp, scale);
+            const int d = (me + 1 + k) % W;
+            uint8_t* dp = ag_sub(p, d, me, sub);
+            put_words<B>(dp, warp, lane, w);
+            if (lane == 0) put_scale(dp, warp, scale);
           }
-          // Own output: decode exactly as the other ranks will.
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(C::decode(codes[j], scale), p.post_scale);
-          store_block<T>(out, elem_base, p.n, vec_out, lane, v);
-        } else if (p.op == kReduceScatter) {
-          const int64_t off = sub * kSubElems + warp * kBlockElems;
-          const int64_t lim = shard_lim(me);
+          // Own output: acc now holds the dequantised codes, bit-identical to
+          // what the other ranks decode from the packed bytes.
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[j] = __fmul_rn(acc[j], p.post_scale);
-          store_block<T>(out, off, lim, vec_out, lane, acc);
-        } else {  // one-shot
-          const int64_t off = sub * kSubElems + warp * kBlockElems;
+          store_block<T>(out, elem_base, p.n, vec_out, lane, acc);
+        } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[j] = __fmul_rn(acc[j], p.post_scale);
-          store_block<T>(out, off, p.n, vec_out, lane, acc);
+          store_block<T>(out, off, p.op == kReduceScatter ? shard_lim(me) : p.n, vec_out, lane, acc);
         }
       }
       if (p.op == kAllReduceTwoShot) {
         __syncthreads();
-        if (threadIdx.x == 0)
-          for (int k = 0; k < W; ++k) {
-            const int dst = (me + 1 + k) % W;
-            signal(p, ag_flag(p, dst, me, c));
-          }
+        if (warp == kThreads / 32 - 1 && lane < W && !skip_signals) {
+          const int d = (me + 1 + lane) % W;
+          st_release_sys(ag_flag(p, d, me, c), p.epoch);
+        }
       }
     } else {
       // ------------------------------------------------------------ phase 3
       const int64_t k3 = item - n1 - n2;
       const int64_t c = k3 / (W - 1);
       const int src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
-      if (threadIdx.x == 0) s_flags[0] = ag_flag(p, me, src, c);
+      if (threadIdx.x == 0) s_ok[cur] = wait_epoch(p, ag_flag(p, me, src, c)) ? 1 : 0;
       __syncthreads();
-      if (!cta_wait(p, s_flags, 1, &s_ok)) break;
-      // all-reduce: the source's shard of the full output; all-gather: the
-      // source's slice of the gathered output (n = per-rank shard elements).
+      if (!s_ok[cur]) break;
+      const bool ag = p.op == kAllGather;
+      const int64_t obase = ag ? static_cast<int64_t>(src) * p.n : static_cast<int64_t>(src) * p.shard_len;
+      const bool vo = vec_out && ((ag ? obase * static_cast<int64_t>(sizeof(T)) : 0) & 15) == 0;
       for (int g = 0; g < p.sub_per_item; ++g) {
         const int64_t sub = c * p.sub_per_item + g;
         if (sub >= p.n_sub) break;
-        const uint8_t* srcp = ag_sub(p, me, src, sub);
+        const uint8_t* sp = ag_sub(p, me, src, sub);
         uint32_t w[B];
-        get_words<B>(srcp, warp, lane, w);
-        const float sc = get_scale(srcp, warp);
-        uint32_t codes[32];
-        unpack32<B>(w, codes);
-        float v[32];
+        get_words<B>(sp, warp, lane, w);
+        const float sc = get_scale(sp, warp);
+        float o[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(C::decode(codes[j], sc), p.post_scale);
-        if (p.op == kAllGather) {
-          store_block<T>(out + src * p.n, sub * kSubElems + warp * kBlockElems, p.n, vec_ag(src),
-                         lane, v);
-        } else {
-          store_block<T>(out, src * p.shard_len + sub * kSubElems + warp * kBlockElems, p.n,
-                         vec_out, lane, v);
-        }
+        for (int j = 0; j < 32; ++j) o[j] = __fmul_rn(C::decode(get_code<B>(w, j), sc), p.post_scale);
+        const int64_t off = sub * kSubElems + warp * kBlockElems;
+        if (ag) store_block<T>(out + obase, off, p.n, vo, lane, o);
+        else store_block<T>(out, obase + off, p.n, vec_out, lane, o);
       }
     }
+    cur ^= 1;
   }
 
   // Exit bookkeeping: the last CTA out resets the launch-local counters.

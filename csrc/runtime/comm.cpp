@@ -175,10 +175,16 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   p.in_stride = in_stride;
   p.shard_valid = shard_valid;
   p.n_sub = n_sub;
-  const int grid_cap = std::max(1, max_ctas > 0 ? std::min(max_ctas, sm_count_) : sm_count_);
+  // Two 256-thread CTAs fit per SM (the kernel is bounded to 128 registers).
+  const int resident = 2 * sm_count_;
+  const int grid_cap = std::max(1, max_ctas > 0 ? std::min(max_ctas, resident) : resident);
   // Items: enough for ~8 per CTA in phase 1, at most 16 sub-chunks each.
   const int64_t phase1_units = (op == kAllReduceTwoShot || op == kReduceScatter) ? world_ * n_sub : n_sub;
-  int64_t spi = phase1_units / (8 * static_cast<int64_t>(grid_cap));
+  // Each item ends with one system-scope release (a fence that waits for the
+  // item's NVLink stores): aim for about three phase-1 items per CTA so the
+  // fence is amortised over several sub-chunks, while small messages keep
+  // one sub-chunk per item for parallelism.
+  int64_t spi = div_up(phase1_units, 3 * static_cast<int64_t>(grid_cap));
   spi = std::max<int64_t>(1, std::min<int64_t>(16, spi));
   p.sub_per_item = static_cast<int>(spi);
   p.n_items_slot = div_up(n_sub, spi);

@@ -47,6 +47,12 @@ setup(
             sources=SOURCES,
             include_dirs=[CSRC],
             extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+            # Link the C++ runtime dynamically: a toolchain that silently
+            # falls back to libstdc++.a would give this module a private copy
+            # of the library (bound locally by -Bsymbolic-functions) that then
+            # mixes with the process's libstdc++ (e.g. its locale facets) and
+            # crashes on the first formatted integer.
+            extra_link_args=["-l:libstdc++.so.6"],
             libraries=["cuda"],
         )
     ],

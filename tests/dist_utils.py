@@ -47,6 +47,9 @@ def _unpack(obj):
 
 
 def _entry(rank, world, port, fn, args, q, env):
+    import faulthandler
+
+    faulthandler.enable(all_threads=True)  # a hard crash prints the Python stacks
     os.environ.update(env)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -98,4 +101,7 @@ def run_ranks(fn, world: int = 2, args=(), timeout: float = 180.0, env=None, all
         results[r] = RuntimeError(val)
     if alive:
         raise AssertionError(f"{len(alive)} rank(s) did not finish within {timeout}s")
+    for r, p in enumerate(procs):
+        if r not in results and r not in allow_fail:
+            raise AssertionError(f"rank {r} exited with code {p.exitcode} without a result")
     return [results.get(r) for r in range(world)]

@@ -118,6 +118,7 @@ def test_fused_reduce_scatter_all_gather():
 def _w_backend(rank, world):
     import bitscom_b200 as bitscom
 
+    bitscom._ext._C.install_crash_backtrace()
     bitscom.init(bitwidth=4, error_feedback=True)
     torch.cuda.set_device(rank)
     dist.init_process_group("lowbit", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))

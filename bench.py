@@ -190,7 +190,7 @@ def build_reference(args, rank, world, local):
         for b, flat in zip(buckets, flats):
             off = 0
             for p in b:
-                flat[off : off + p.numel()].copy_(p.grad.view(-1))
+                flat[off : off + p.numel()].copy_(p.grad.reshape(-1))
                 off += p.numel()
             if group is None:
                 dist.all_reduce(flat).wait()
@@ -199,7 +199,7 @@ def build_reference(args, rank, world, local):
             flat.div_(world)
             off = 0
             for p in b:
-                p.grad.copy_(flat[off : off + p.numel()].view_as(p.grad))
+                p.grad.copy_(flat[off : off + p.numel()].view(p.grad.shape))
                 off += p.numel()
 
     def step(x, y):

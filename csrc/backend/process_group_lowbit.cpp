@@ -679,7 +679,8 @@ c10::intrusive_ptr<c10d::Backend> createProcessGroupLowBit(const c10::intrusive_
 void register_backend_bindings(pybind11::module& m) {
   namespace py = pybind11;
   py::module::import("torch.distributed");
-  py::class_<LowBitOptions>(m, "LowBitOptions")
+  // module_local: the reference package registers classes with the same names.
+  py::class_<LowBitOptions>(m, "LowBitOptions", py::module_local())
       .def(py::init<>())
       .def_readwrite("bitwidth", &LowBitOptions::bitwidth)
       .def_readwrite("error_feedback", &LowBitOptions::error_feedback)
@@ -693,7 +694,8 @@ void register_backend_bindings(pybind11::module& m) {
       .def_readwrite("seed", &LowBitOptions::seed)
       .def_readwrite("blocking_wait", &LowBitOptions::blocking_wait);
 
-  py::class_<ProcessGroupLowBit, c10d::Backend, c10::intrusive_ptr<ProcessGroupLowBit>>(m, "ProcessGroupLowBit")
+  py::class_<ProcessGroupLowBit, c10d::Backend, c10::intrusive_ptr<ProcessGroupLowBit>>(m, "ProcessGroupLowBit",
+                                                                                      py::module_local())
       .def(py::init([](const c10::intrusive_ptr<c10d::Store>& store, int rank, int size,
                        c10::intrusive_ptr<c10d::Backend> cpu_inner, c10::intrusive_ptr<c10d::Backend> cuda_inner,
                        LowBitOptions options) {

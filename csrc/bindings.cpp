@@ -254,7 +254,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("packed_bytes", [](int64_t n, int64_t bits) -> int64_t { return packed_bytes_ref(n, static_cast<int>(bits)); });
   m.def("wire_sub_bytes", [](int64_t bits) -> int64_t { return launch::coll_sub_bytes(static_cast<int>(bits)); });
 
-  py::class_<CollStats>(m, "CollStats")
+  // module_local: another extension in the process (e.g. the reference package)
+  // may register classes with the same names.
+  py::class_<CollStats>(m, "CollStats", py::module_local())
       .def_readonly("calls", &CollStats::calls)
       .def_readonly("launches", &CollStats::launches)
       .def_readonly("elements", &CollStats::elements)
@@ -262,7 +264,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readonly("oneshot", &CollStats::oneshot)
       .def_readonly("twoshot", &CollStats::twoshot);
 
-  py::class_<LowBitComm, std::shared_ptr<LowBitComm>>(m, "LowBitComm")
+  py::class_<LowBitComm, std::shared_ptr<LowBitComm>>(m, "LowBitComm", py::module_local())
       .def(py::init<int, int, int, int64_t>(), py::arg("rank"), py::arg("world"), py::arg("device"),
            py::arg("workspace_bytes"))
       .def_property_readonly("rank", &LowBitComm::rank)

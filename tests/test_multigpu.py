@@ -119,7 +119,7 @@ def _w_backend(rank, world):
     import bitscom_b200 as bitscom
 
     bitscom._ext._C.install_crash_backtrace()
-    bitscom.init(bitwidth=4, error_feedback=True)
+    bitscom.init(bitwidth=4, error_feedback=True, algo="twoshot")
     torch.cuda.set_device(rank)
     dist.init_process_group("lowbit", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     x = _x(200000, rank, seed=9).cuda()

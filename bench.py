@@ -193,7 +193,7 @@ def build_reference(args, rank, world, local):
                 flat[off : off + p.numel()].copy_(p.grad.reshape(-1))
                 off += p.numel()
             if group is None:
-                dist.all_reduce(flat).wait()
+                dist.all_reduce(flat)  # synchronous: waits on the reference's Work (runs its second phase)
             else:
                 group.all_reduce(flat, async_op=False)
             flat.div_(world)

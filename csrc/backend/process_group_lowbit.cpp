@@ -15,7 +15,7 @@
 #include <cstdlib>
 #include <stdexcept>
 
-namespace bitscom {
+namespace bitscom_b200 {
 namespace {
 
 std::pair<int, int> quant_bounds(int bits) {
@@ -149,6 +149,26 @@ ProcessGroupLowBit::ProcessGroupLowBit(const c10::intrusive_ptr<c10d::Store>& st
 }
 
 ProcessGroupLowBit::~ProcessGroupLowBit() = default;
+
+void ProcessGroupLowBit::shutdown() {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    recent_.clear();
+    comms_.clear();
+    p2p_ok_.clear();
+    residuals_.clear();
+  }
+  if (cuda_inner_) cuda_inner_->shutdown();
+  if (cpu_inner_) cpu_inner_->shutdown();
+  cuda_inner_.reset();
+  cpu_inner_.reset();
+}
+
+void ProcessGroupLowBit::abort() {
+  if (cuda_inner_) cuda_inner_->abort();
+  if (cpu_inner_) cpu_inner_->abort();
+  shutdown();
+}
 
 c10::intrusive_ptr<c10d::Backend> ProcessGroupLowBit::inner(const at::Tensor& t) const {
   if (t.is_cuda()) {
@@ -679,8 +699,9 @@ c10::intrusive_ptr<c10d::Backend> createProcessGroupLowBit(const c10::intrusive_
 void register_backend_bindings(pybind11::module& m) {
   namespace py = pybind11;
   py::module::import("torch.distributed");
-  // module_local: the reference package registers classes with the same names.
-  py::class_<LowBitOptions>(m, "LowBitOptions", py::module_local())
+  // The C++ namespace (bitscom_b200) keeps these types distinct from the
+  // reference's same-named classes when both extensions share a process.
+  py::class_<LowBitOptions>(m, "LowBitOptions")
       .def(py::init<>())
       .def_readwrite("bitwidth", &LowBitOptions::bitwidth)
       .def_readwrite("error_feedback", &LowBitOptions::error_feedback)
@@ -694,8 +715,7 @@ void register_backend_bindings(pybind11::module& m) {
       .def_readwrite("seed", &LowBitOptions::seed)
       .def_readwrite("blocking_wait", &LowBitOptions::blocking_wait);
 
-  py::class_<ProcessGroupLowBit, c10d::Backend, c10::intrusive_ptr<ProcessGroupLowBit>>(m, "ProcessGroupLowBit",
-                                                                                      py::module_local())
+  py::class_<ProcessGroupLowBit, c10d::Backend, c10::intrusive_ptr<ProcessGroupLowBit>>(m, "ProcessGroupLowBit")
       .def(py::init([](const c10::intrusive_ptr<c10d::Store>& store, int rank, int size,
                        c10::intrusive_ptr<c10d::Backend> cpu_inner, c10::intrusive_ptr<c10d::Backend> cuda_inner,
                        LowBitOptions options) {
@@ -712,4 +732,4 @@ void register_backend_bindings(pybind11::module& m) {
       .def("communicator", &ProcessGroupLowBit::comm, py::call_guard<py::gil_scoped_release>());
 }
 
-}  // namespace bitscom
+}  // namespace bitscom_b200

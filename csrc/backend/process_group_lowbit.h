@@ -41,7 +41,7 @@
 
 #include "../runtime/comm.h"
 
-namespace bitscom {
+namespace bitscom_b200 {
 
 struct LowBitOptions {
   // Reference options (cpp/include/process_group_lowbit.h:20-24).
@@ -145,6 +145,11 @@ class ProcessGroupLowBit : public c10d::Backend {
   void setSequenceNumberForGroup() override;
   uint64_t getSequenceNumberForGroup() override;
   void setTimeout(std::chrono::milliseconds timeout) override { options_.timeout = timeout; }
+  // destroy_process_group(): shut the inner backends down and release the
+  // fused-path workspaces now, not whenever the last Python reference to this
+  // backend goes away (by then the peers may have exited).
+  void shutdown() override;
+  void abort() override;
 
   // Introspection (exposed to Python).
   std::map<std::string, int64_t> stats() const;
@@ -191,4 +196,4 @@ c10::intrusive_ptr<c10d::Backend> createProcessGroupLowBit(
 
 void register_backend_bindings(pybind11::module& m);
 
-}  // namespace bitscom
+}  // namespace bitscom_b200

@@ -19,7 +19,7 @@
 #include "kernels/launchers.h"
 #include "runtime/comm.h"
 
-namespace bitscom {
+namespace bitscom_b200 {
 namespace {
 
 // Debug aid: on SIGSEGV/SIGABRT print the native call stack (glibc
@@ -234,10 +234,10 @@ void comm_all_gather(LowBitComm& c, const at::Tensor& in, at::Tensor& out, const
 }
 
 }  // namespace
-}  // namespace bitscom
+}  // namespace bitscom_b200
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  using namespace bitscom;
+  using namespace bitscom_b200;
   m.doc() = "bitscom_b200 native extension: sm_100a low-bit kernels, fused NVLink collectives, lowbit c10d backend";
   m.def("absmax", &absmax_op, py::arg("x"), py::arg("residual") = py::none());
   m.def("quantize", &quantize_op, py::arg("x"), py::arg("bits"), py::arg("stochastic") = false,
@@ -254,9 +254,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("packed_bytes", [](int64_t n, int64_t bits) -> int64_t { return packed_bytes_ref(n, static_cast<int>(bits)); });
   m.def("wire_sub_bytes", [](int64_t bits) -> int64_t { return launch::coll_sub_bytes(static_cast<int>(bits)); });
 
-  // module_local: another extension in the process (e.g. the reference package)
-  // may register classes with the same names.
-  py::class_<CollStats>(m, "CollStats", py::module_local())
+  py::class_<CollStats>(m, "CollStats")
       .def_readonly("calls", &CollStats::calls)
       .def_readonly("launches", &CollStats::launches)
       .def_readonly("elements", &CollStats::elements)
@@ -264,7 +262,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readonly("oneshot", &CollStats::oneshot)
       .def_readonly("twoshot", &CollStats::twoshot);
 
-  py::class_<LowBitComm, std::shared_ptr<LowBitComm>>(m, "LowBitComm", py::module_local())
+  py::class_<LowBitComm, std::shared_ptr<LowBitComm>>(m, "LowBitComm")
       .def(py::init<int, int, int, int64_t>(), py::arg("rank"), py::arg("world"), py::arg("device"),
            py::arg("workspace_bytes"))
       .def_property_readonly("rank", &LowBitComm::rank)

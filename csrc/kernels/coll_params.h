@@ -4,7 +4,7 @@
 
 #include <stdint.h>
 
-namespace bitscom {
+namespace bitscom_b200 {
 
 constexpr int kMaxRanks = 8;          // one NVSwitch node
 constexpr int kBlockElems = 1024;     // elements per quantisation block (one warp)
@@ -79,4 +79,4 @@ struct CollParams {
   uint64_t timeout_ns;
 };
 
-}  // namespace bitscom
+}  // namespace bitscom_b200

@@ -21,7 +21,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-namespace bitscom {
+namespace bitscom_b200 {
 
 // ---------------------------------------------------------------------------
 // Quantisation bounds
@@ -206,4 +206,4 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   return __ldcg(reinterpret_cast<const uint4*>(p));
 }
 
-}  // namespace bitscom
+}  // namespace bitscom_b200

@@ -9,7 +9,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-namespace bitscom {
+namespace bitscom_b200 {
 
 enum DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
@@ -69,11 +69,11 @@ void absmax_sum(const void* x, DType dt, const float* residual, int64_t n, uint3
                 cudaStream_t s);
 
 }  // namespace launch
-}  // namespace bitscom
+}  // namespace bitscom_b200
 
 #include "coll_params.h"
 
-namespace bitscom {
+namespace bitscom_b200 {
 namespace launch {
 
 // Bytes of one packed sub-chunk (8 x 1024 elements) at `bits` per element.
@@ -87,4 +87,4 @@ void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t
 cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s);
 
 }  // namespace launch
-}  // namespace bitscom
+}  // namespace bitscom_b200

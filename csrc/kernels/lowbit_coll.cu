@@ -48,7 +48,7 @@
 #include <stdexcept>
 #include <string>
 
-namespace bitscom {
+namespace bitscom_b200 {
 namespace {
 
 constexpr int kThreads = 256;  // 8 warps = one sub-chunk per CTA pass
@@ -573,4 +573,4 @@ cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int gri
 }
 
 }  // namespace launch
-}  // namespace bitscom
+}  // namespace bitscom_b200

@@ -24,8 +24,8 @@
 namespace {
 
 constexpr long long kMaxElems = 1ll << 20;                    // 1,048,576 elements
-constexpr long long kMaxSubs = kMaxElems / bitscom::kSubElems;  // 128 sub-chunks
-constexpr long long kMaxSubBytes = bitscom::kHeaderBytes + bitscom::kSubBlocks * 128ll * 16;  // 16-bit
+constexpr long long kMaxSubs = kMaxElems / bitscom_b200::kSubElems;  // 128 sub-chunks
+constexpr long long kMaxSubBytes = bitscom_b200::kHeaderBytes + bitscom_b200::kSubBlocks * 128ll * 16;  // 16-bit
 constexpr long long kCounterBytes = 4096;
 constexpr long long kFlagBytes = 4 * kMaxSubs * 4;
 constexpr long long kDataOff = kCounterBytes + ((kFlagBytes + 255) / 256) * 256;
@@ -79,7 +79,7 @@ __attribute__((visibility("default"))) const char* bitscom_noalloc_strerror(int 
 __attribute__((visibility("default"))) int bitscom_lowbit_allreduce_local_noalloc(
     const void* in, void* out, float* residual, long long n, int dtype, int bits, float post_scale,
     void* stream_ptr) {
-  using namespace bitscom;
+  using namespace bitscom_b200;
   if (n < 0 || in == nullptr || out == nullptr) return BITSCOM_NOALLOC_EINVAL;
   if (dtype < 0 || dtype > 2) return BITSCOM_NOALLOC_EINVAL;
   if (bits != 1 && bits != 2 && bits != 4 && bits != 8 && bits != 12 && bits != 16) return BITSCOM_NOALLOC_EINVAL;

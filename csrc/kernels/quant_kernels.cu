@@ -23,7 +23,7 @@
 #include <stdexcept>
 #include <string>
 
-namespace bitscom {
+namespace bitscom_b200 {
 namespace {
 
 constexpr int kWarps = 8;
@@ -603,4 +603,4 @@ void ef_roundtrip_ref(const void* x, DType dt, int64_t n, int bits, float* resid
 }
 
 }  // namespace launch
-}  // namespace bitscom
+}  // namespace bitscom_b200

@@ -16,7 +16,7 @@
 #include <stdexcept>
 #include <string>
 
-namespace bitscom {
+namespace bitscom_b200 {
 namespace {
 
 void ck(cudaError_t e, const char* what) {
@@ -308,4 +308,4 @@ void LowBitComm::all_gather(const void* in, void* out, float* residual, int64_t 
          offset, 1.0f, s, max_ctas);
 }
 
-}  // namespace bitscom
+}  // namespace bitscom_b200

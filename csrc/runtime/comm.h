@@ -24,7 +24,7 @@
 #include "../kernels/coll_params.h"
 #include "../kernels/launchers.h"
 
-namespace bitscom {
+namespace bitscom_b200 {
 
 enum Algo : int { kAlgoAuto = 0, kAlgoTwoShot = 1, kAlgoOneShot = 2 };
 
@@ -115,4 +115,4 @@ class LowBitComm {
   CollStats stats_;
 };
 
-}  // namespace bitscom
+}  // namespace bitscom_b200

@@ -50,6 +50,8 @@ def _entry(rank, world, port, fn, args, q, env):
     import faulthandler
 
     faulthandler.enable(all_threads=True)  # a hard crash prints the Python stacks
+    if env.get("BITSCOM_TEST_DUMP_AFTER"):  # debugging aid: dump stacks of a hung rank
+        faulthandler.dump_traceback_later(float(env["BITSCOM_TEST_DUMP_AFTER"]), exit=False)
     os.environ.update(env)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)

@@ -183,7 +183,7 @@ def _w_backend(rank, world, bits, ef):
 
 @pytest.mark.parametrize("bits,ef", [(4, False), (2, True), (1, False)])
 def test_native_backend_staged_path(bits, ef):
-    res = run_ranks(_w_backend, 2, (bits, ef))
+    res = run_ranks(_w_backend, 2, (bits, ef), env={"BITSCOM_TEST_DUMP_AFTER": os.environ.get("BITSCOM_TEST_DUMP_AFTER", "")})
     inputs = [r[0] for r in res]
     residuals = [torch.zeros(inputs[0].numel()) for _ in inputs] if ef else None
     for step in range(3):

@@ -74,18 +74,31 @@ def setup(args):
     return rank, world, local
 
 
+# Group used for timing barriers and max-over-ranks reductions: plain NCCL, so
+# the reference arm (whose backend implements neither barrier nor MAX) is
+# timed the same way as ours.
+_AUX = None
+
+
+def aux_group():
+    global _AUX
+    if _AUX is None:
+        _AUX = dist.new_group(backend="nccl")
+    return _AUX
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=aux_group())
     return float(t.item())
 
 
 def barrier_sync(world):
     torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
+        dist.barrier(group=aux_group(), device_ids=[torch.cuda.current_device()])
     torch.cuda.synchronize()
 
 
@@ -323,7 +336,8 @@ def main():
             out["e2e"] = e2e
         print(json.dumps(out), flush=True)
     if dist.is_initialized():
-        dist.barrier()
+        if world > 1:
+            dist.barrier(group=aux_group(), device_ids=[torch.cuda.current_device()])
         dist.destroy_process_group()
 
 

@@ -52,7 +52,12 @@ def parse():
     p.add_argument("--batch", type=int, default=256)
     p.add_argument("--bits", type=int, default=4)
     p.add_argument("--bucket-mb", type=float, default=25.0)
-    p.add_argument("--max-ctas", type=int, default=0)
+    p.add_argument("--max-ctas", type=int, default=0, help="CTAs of each fused launch (0 = library default)")
+    p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot"])
+    p.add_argument("--hook", default="lowbit", choices=["lowbit", "none"],
+                   help="diagnostic: 'none' runs DDP's own fp32 NCCL all-reduce")
+    p.add_argument("--no-broadcast-buffers", action="store_true",
+                   help="diagnostic: skip DDP's per-forward buffer broadcast")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--ref-path", choices=["ef", "python"], default="ef",
                    help="reference arm: its C++ error-feedback backend path, or its Python LowBitGroup path")
@@ -125,7 +130,12 @@ def build_ours(args, rank, world, local):
         model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True,
         process_group=dist.group.WORLD,
     )
-    state = bitscom.register_lowbit_hook(ddp, bitwidth=args.bits, error_feedback=True, max_ctas=args.max_ctas)
+    if args.hook == "lowbit":
+        state = bitscom.register_lowbit_hook(ddp, bitwidth=args.bits, error_feedback=True, max_ctas=args.max_ctas,
+                                             algo=args.algo)
+    else:  # diagnostic: DDP's own fp32 NCCL all-reduce
+        state = bitscom.LowBitHookState()
+    ddp.broadcast_buffers = not args.no_broadcast_buffers
     opt = torch.optim.SGD(ddp.parameters(), lr=0.1, momentum=0.9, fused=True)
 
     def step(x, y):
@@ -322,7 +332,9 @@ def main():
                 "seq_len": None,
                 "image": [3, 32, 32],
                 "parallelism": f"dp{world}",
-                "comm": f"{args.bits}-bit error-feedback low-bit all-reduce, {args.bucket_mb} MB buckets",
+                "comm": (f"{args.bits}-bit error-feedback low-bit all-reduce, {args.bucket_mb} MB buckets"
+                         if args.hook == "lowbit" or args.impl == "reference"
+                         else f"fp32 NCCL all-reduce (diagnostic), {args.bucket_mb} MB buckets"),
                 "optimizer": "SGD momentum 0.9",
                 "l2": f"rotating pool of {POOL} device-resident batches ({POOL * 3} MiB > 126 MiB L2)",
                 "implementation": desc,

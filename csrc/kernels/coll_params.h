@@ -47,6 +47,7 @@ struct CollParams {
   int64_t shard_len;   // elements per shard on the wire, a multiple of kSubElems
   int64_t in_stride;   // distance between shard starts in the input (all-reduce / reduce-scatter)
   int64_t shard_valid; // elements of each shard that exist in the input
+  int64_t out_stride;  // all-gather: distance between source slices in the output
   int64_t n_sub;       // sub-chunks per slot (per shard; per tensor for one-shot)
   int sub_per_item;    // sub-chunks handled by one work item (one flag each)
   int64_t n_items_slot;  // items per slot = ceil(n_sub / sub_per_item)

@@ -401,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
             float o[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) o[j] = C::decode(get_code<B>(w, j), scale);
-            const bool va = vec_out && ((static_cast<int64_t>(me) * p.n * static_cast<int64_t>(sizeof(T))) & 15) == 0;
-            store_block<T>(out + static_cast<int64_t>(me) * p.n, off, p.n, va, lane, o);
+            const bool va = vec_out && ((static_cast<int64_t>(me) * p.out_stride * static_cast<int64_t>(sizeof(T))) & 15) == 0;
+            store_block<T>(out + static_cast<int64_t>(me) * p.out_stride, off, p.n, va, lane, o);
           }
         }
       }
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
       __syncthreads();
       if (!s_ok[cur]) break;
       const bool ag = p.op == kAllGather;
-      const int64_t obase = ag ? static_cast<int64_t>(src) * p.n : static_cast<int64_t>(src) * p.shard_len;
+      const int64_t obase = ag ? static_cast<int64_t>(src) * p.out_stride : static_cast<int64_t>(src) * p.shard_len;
       const bool vo = vec_out && ((ag ? obase * static_cast<int64_t>(sizeof(T)) : 0) & 15) == 0;
       for (int g = 0; g < p.sub_per_item; ++g) {
         const int64_t sub = c * p.sub_per_item + g;

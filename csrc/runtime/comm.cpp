@@ -159,7 +159,7 @@ void LowBitComm::set_fault_skip_signal(bool on) {
 void LowBitComm::launch(int op, const void* in, void* out, float* residual, int64_t n,
                         int64_t shard_len, int64_t in_stride, int64_t shard_valid, int64_t n_sub, DType dt, int bits, int fmt, bool sr,
                         bool sr2, uint64_t seed, uint64_t offset, float post_scale, cudaStream_t s,
-                        int max_ctas) {
+                        int max_ctas, int64_t out_stride) {
   const Layout L = layout(bits);
   CollParams p;
   std::memset(&p, 0, sizeof(p));
@@ -174,6 +174,7 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   p.shard_len = shard_len;
   p.in_stride = in_stride;
   p.shard_valid = shard_valid;
+  p.out_stride = out_stride > 0 ? out_stride : n;
   p.n_sub = n_sub;
   // Two 256-thread CTAs fit per SM (the kernel is bounded to 128 registers).
   const int resident = 2 * sm_count_;
@@ -261,13 +262,13 @@ void LowBitComm::allreduce(const void* in, void* out, float* residual, int64_t n
       stats_.oneshot += 1;
       const int64_t n_sub = div_up(m, kSubElems);
       launch(op, ip, op_, rp, m, n_sub * kSubElems, 0, m, n_sub, dt, bits, fmt, sr, sr_requant, seed,
-             offset + static_cast<uint64_t>(off), post_scale, s, max_ctas);
+             offset + static_cast<uint64_t>(off), post_scale, s, max_ctas, 0);
     } else {
       stats_.twoshot += 1;
       const int64_t shard = div_up(div_up(m, world_), kSubElems) * kSubElems;
       const int64_t n_sub = shard / kSubElems;
       launch(op, ip, op_, rp, m, shard, shard, shard, n_sub, dt, bits, fmt, sr, sr_requant, seed,
-             offset + static_cast<uint64_t>(off), post_scale, s, max_ctas);
+             offset + static_cast<uint64_t>(off), post_scale, s, max_ctas, 0);
     }
   }
 }
@@ -279,15 +280,19 @@ void LowBitComm::reduce_scatter(const void* in, void* out, float* residual, int6
   if (shard <= 0) return;
   stats_.calls += 1;
   stats_.elements += static_cast<uint64_t>(shard) * world_;
-  const int64_t shard_pad = div_up(shard, kSubElems) * kSubElems;
-  const int64_t cap = max_elems_per_launch(kReduceScatter, bits) / world_;
-  if (shard_pad > cap) {
-    throw std::runtime_error("bitscom: reduce_scatter shard of " + std::to_string(shard) +
-                             " elements exceeds the workspace capacity of " + std::to_string(cap) +
-                             " (raise BITSCOM_WORKSPACE_MB)");
+  const int esz = dt == kF32 ? 4 : 2;
+  // Shards larger than one launch's slot capacity are processed as column
+  // segments [a, a+m) of every rank's shard (input stride stays `shard`).
+  const int64_t cap = (max_elems_per_launch(kReduceScatter, bits) / world_) / kSubElems * kSubElems;
+  if (cap <= 0) throw std::runtime_error("bitscom: workspace too small for this bitwidth");
+  for (int64_t a = 0; a < shard; a += cap) {
+    const int64_t m = std::min(cap, shard - a);
+    const int64_t m_pad = div_up(m, kSubElems) * kSubElems;
+    launch(kReduceScatter, static_cast<const char*>(in) + a * esz, static_cast<char*>(out) + a * esz,
+           residual ? residual + a : nullptr, static_cast<int64_t>(world_ - 1) * shard + m, m_pad, shard, m,
+           m_pad / kSubElems, dt, bits, fmt, sr, false, seed, offset + static_cast<uint64_t>(a), post_scale, s,
+           max_ctas, 0);
   }
-  launch(kReduceScatter, in, out, residual, shard * world_, shard_pad, shard, shard, shard_pad / kSubElems,
-         dt, bits, fmt, sr, false, seed, offset, post_scale, s, max_ctas);
 }
 
 void LowBitComm::all_gather(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
@@ -297,15 +302,18 @@ void LowBitComm::all_gather(const void* in, void* out, float* residual, int64_t 
   if (shard <= 0) return;
   stats_.calls += 1;
   stats_.elements += static_cast<uint64_t>(shard) * world_;
-  const int64_t cap = max_elems_per_launch(kAllGather, bits);
-  if (shard > cap) {
-    throw std::runtime_error("bitscom: all_gather shard of " + std::to_string(shard) +
-                             " elements exceeds the workspace capacity of " + std::to_string(cap) +
-                             " (raise BITSCOM_WORKSPACE_MB)");
+  const int esz = dt == kF32 ? 4 : 2;
+  // Large shards: segments [a, a+m) of every rank's slice; the output keeps
+  // the rank-major layout through out_stride = shard.
+  const int64_t cap = max_elems_per_launch(kAllGather, bits) / kSubElems * kSubElems;
+  if (cap <= 0) throw std::runtime_error("bitscom: workspace too small for this bitwidth");
+  for (int64_t a = 0; a < shard; a += cap) {
+    const int64_t m = std::min(cap, shard - a);
+    const int64_t n_sub = div_up(m, kSubElems);
+    launch(kAllGather, static_cast<const char*>(in) + a * esz, static_cast<char*>(out) + a * esz,
+           residual ? residual + a : nullptr, m, n_sub * kSubElems, 0, m, n_sub, dt, bits, fmt, sr, false, seed,
+           offset + static_cast<uint64_t>(a), 1.0f, s, max_ctas, shard);
   }
-  const int64_t n_sub = div_up(shard, kSubElems);
-  launch(kAllGather, in, out, residual, shard, n_sub * kSubElems, 0, shard, n_sub, dt, bits, fmt, sr, false, seed,
-         offset, 1.0f, s, max_ctas);
 }
 
 }  // namespace bitscom_b200

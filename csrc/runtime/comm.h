@@ -95,7 +95,7 @@ class LowBitComm {
   Layout layout(int bits) const;
   void launch(int op, const void* in, void* out, float* residual, int64_t n, int64_t shard_len,
               int64_t in_stride, int64_t shard_valid, int64_t n_sub, DType dt, int bits, int fmt, bool sr, bool sr2, uint64_t seed,
-              uint64_t offset, float post_scale, cudaStream_t s, int max_ctas);
+              uint64_t offset, float post_scale, cudaStream_t s, int max_ctas, int64_t out_stride);
   void ensure_usable() const;
 
   int rank_, world_, device_;

@@ -147,3 +147,54 @@ def test_timeout_returns_error_status_without_faulting(cuda):
     # the CUDA context is still healthy
     y = torch.ones(10, device="cuda") * 2
     assert float(y.sum()) == 20.0
+
+
+def test_segmented_reduce_scatter_and_all_gather(comm):
+    """Shards larger than one launch are processed as column segments."""
+    cap_ag = comm.native.max_elems_per_launch(3, 8)
+    n = cap_ag + 5 * 8192 + 77
+    x = _x(n, seed=21)
+    g = torch.empty(n, device="cuda")
+    r = torch.zeros(n, device="cuda")
+    comm.all_gather(g, x.cuda(), bits=8, residual=r)
+    out = torch.empty(n, device="cuda")
+    comm.reduce_scatter(out, x.cuda(), bits=8)
+    torch.cuda.synchronize()
+    assert torch.equal(g.cpu(), emu.all_gather([x], 8))
+    assert torch.equal(out.cpu(), emu.reduce_scatter([x], 8)[0])
+    # residual of the gather = x - dequant(quant(x))
+    assert torch.equal(r.cpu(), x - emu.all_gather([x], 8))
+
+
+def test_sharded_dp_single_rank_trains(cuda):
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from bitscom_b200.models import gpt2_small_test
+    from bitscom_b200.parallel.fsdp import LowBitShardedDP
+
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29653")
+        dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+    torch.manual_seed(0)
+    model = gpt2_small_test(n_positions=128).cuda()
+    sdp = LowBitShardedDP(model, lambda ps: torch.optim.AdamW(ps, lr=1e-3), rs_bits=8, ag_bits=8)
+    start = torch.randint(0, 512, (8, 1), device="cuda")
+    tok = (start + torch.arange(65, device="cuda")) % 512
+    losses = []
+    for _ in range(30):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            _, loss = sdp(tok[:, :-1], tok[:, 1:])
+        loss.backward()
+        sdp.step()
+        losses.append(float(loss))
+    assert losses[-1] < losses[0] - 1.0
+    assert torch.isfinite(sdp.flat_param).all()
+    # working parameters = decoded master (+ the all-gather residual keeps the difference small)
+    lo = sdp.rank * sdp.shard
+    diff = (sdp.flat_param[lo : lo + sdp.shard] - sdp.master.detach()).abs().max()
+    assert float(diff) < 0.02 * float(sdp.master.detach().abs().max())
+    dist.destroy_process_group()

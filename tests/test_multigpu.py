@@ -254,3 +254,34 @@ def test_pipeline_a_on_gpus():
     y, exp, ga = res[0]
     assert torch.equal(ga[0], ga[1])
     assert (y - exp).abs().max() / exp.abs().max() < 0.2
+
+
+def _w_sdp(rank, world):
+    from bitscom_b200.models import gpt2_small_test
+    from bitscom_b200.parallel.fsdp import LowBitShardedDP
+
+    _init(rank, world)
+    torch.manual_seed(0)
+    model = gpt2_small_test(n_positions=128).cuda()
+    sdp = LowBitShardedDP(model, lambda ps: torch.optim.AdamW(ps, lr=1e-3), rs_bits=8, ag_bits=8)
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    losses = []
+    for _ in range(20):
+        start = torch.randint(0, 512, (8, 1), device="cuda", generator=g)
+        tok = (start + torch.arange(65, device="cuda")) % 512
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            _, loss = sdp(tok[:, :-1], tok[:, 1:])
+        loss.backward()
+        sdp.step()
+        losses.append(float(loss))
+    torch.cuda.synchronize()
+    fp = sdp.flat_param.cpu()
+    dist.destroy_process_group()
+    return fp, losses
+
+
+def test_sharded_dp_replicas_identical():
+    _need(2)
+    res = run_ranks(_w_sdp, 2, env=ENV, timeout=300)
+    assert torch.equal(res[0][0], res[1][0])  # every rank decodes the same gathered bytes
+    assert res[0][1][-1] < res[0][1][0]

@@ -1,0 +1,51 @@
+"""Trace analyzer, EF-benchmark arithmetic and the sharded-DP module on CPU."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from bitscom_b200.utils.trace import analyze, step_window
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _trace():
+    ev = []
+    for i in range(4):
+        t0 = i * 1000
+        ev.append({"ph": "X", "name": f"ProfilerStep#{i}", "ts": t0, "dur": 900})
+        ev.append({"ph": "X", "name": "aten::conv2d", "ts": t0 + 10, "dur": 500, "cat": "cpu_op"})
+        ev.append({"ph": "X", "name": "lowbit_coll_kernel<float, 4, 0>", "ts": t0 + 600, "dur": 200, "cat": "kernel"})
+        ev.append({"ph": "X", "name": "nccl:broadcast", "ts": t0 + 820, "dur": 50, "cat": "cpu_op"})
+    return ev
+
+
+def test_trace_window_and_comm_share():
+    ev = _trace()
+    w = step_window(ev, skip_steps=1, keep_steps=2)
+    assert w.start_us == 1000 and w.end_us == 2900
+    res = analyze(ev, w)
+    assert res["total_op_us"] == 2 * 750 and res["comm_us"] == 2 * 250
+    assert abs(res["comm_share"] - 250 / 750) < 1e-9
+    gpu = analyze(ev, w, gpu_only=True)
+    assert gpu["comm_share"] == 1.0
+
+
+def test_trace_cli(tmp_path):
+    path = tmp_path / "t.json"
+    path.write_text(json.dumps({"traceEvents": _trace()}))
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "benchmarks", "analyze_trace.py"), str(path)],
+                         capture_output=True, text=True, check=True).stdout
+    assert json.loads(out.splitlines()[0])["comm_us"] == 3 * 250
+
+
+def test_ef_benefit_curve_cpu_shows_ef_gain():
+    sys.path.insert(0, os.path.join(ROOT, "benchmarks"))
+    from error_feedback_comparison import ef_benefit_curve
+
+    rows = ef_benefit_curve(torch.device("cpu"), 4, 40, 1 << 14, 0)
+    assert rows[-1][2] < rows[-1][1] / 3  # EF cumulative error far below no-EF

@@ -52,12 +52,14 @@ def parse():
     p.add_argument("--batch", type=int, default=256)
     p.add_argument("--bits", type=int, default=4)
     p.add_argument("--bucket-mb", type=float, default=25.0)
-    p.add_argument("--max-ctas", type=int, default=0, help="CTAs of each fused launch (0 = library default)")
+    p.add_argument("--max-ctas", type=int, default=None,
+                   help="CTAs of each fused launch (default: the hook's default; 0 = two per SM)")
     p.add_argument("--algo", default="auto", choices=["auto", "oneshot", "twoshot"])
     p.add_argument("--hook", default="lowbit", choices=["lowbit", "none"],
                    help="diagnostic: 'none' runs DDP's own fp32 NCCL all-reduce")
-    p.add_argument("--no-broadcast-buffers", action="store_true",
-                   help="diagnostic: skip DDP's per-forward buffer broadcast")
+    p.add_argument("--broadcast-buffers", action="store_true",
+                   help="broadcast BatchNorm buffers from rank 0 before every forward (DDP's default); off by default "
+                        "because the reference's training loop synchronises gradients only")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--ref-path", choices=["ef", "python"], default="ef",
                    help="reference arm: its C++ error-feedback backend path, or its Python LowBitGroup path")
@@ -131,11 +133,11 @@ def build_ours(args, rank, world, local):
         process_group=dist.group.WORLD,
     )
     if args.hook == "lowbit":
-        state = bitscom.register_lowbit_hook(ddp, bitwidth=args.bits, error_feedback=True, max_ctas=args.max_ctas,
-                                             algo=args.algo)
+        extra = {} if args.max_ctas is None else {"max_ctas": args.max_ctas}
+        state = bitscom.register_lowbit_hook(ddp, bitwidth=args.bits, error_feedback=True, algo=args.algo, **extra)
     else:  # diagnostic: DDP's own fp32 NCCL all-reduce
         state = bitscom.LowBitHookState()
-    ddp.broadcast_buffers = not args.no_broadcast_buffers
+    ddp.broadcast_buffers = args.broadcast_buffers
     opt = torch.optim.SGD(ddp.parameters(), lr=0.1, momentum=0.9, fused=True)
 
     def step(x, y):
@@ -336,6 +338,8 @@ def main():
                          if args.hook == "lowbit" or args.impl == "reference"
                          else f"fp32 NCCL all-reduce (diagnostic), {args.bucket_mb} MB buckets"),
                 "optimizer": "SGD momentum 0.9",
+                "buffer_sync": ("DDP broadcast of BatchNorm buffers every forward" if args.broadcast_buffers
+                                else "none (gradients only, as in the reference's loop)"),
                 "l2": f"rotating pool of {POOL} device-resident batches ({POOL * 3} MiB > 126 MiB L2)",
                 "implementation": desc,
             },

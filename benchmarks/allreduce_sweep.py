@@ -75,6 +75,8 @@ def main():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--max-ctas", type=int, default=0)
+    p.add_argument("--lag", type=int, nargs="+", default=[-1],
+                   help="schedule lags to sweep (-1 automatic, 0 phase-major)")
     args = p.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -112,7 +114,10 @@ def main():
         x0 = gradient_like(n, rank, "cuda")
         buf = x0.clone()
         bus_factor = 2.0 * (world - 1) / world if world > 1 else 1.0
-        for impl in args.impls:
+        runs = [(impl, lag) for impl in args.impls for lag in (args.lag if impl == "ours" else [None])]
+        for impl, lag in runs:
+            if lag is not None:
+                comm.set_schedule_lag(lag)
             for bits, fmt in formats if impl != "nccl" else [(32, "fp32")]:
                 if impl == "nccl":
                     fn = lambda: dist.all_reduce(buf)
@@ -157,6 +162,7 @@ def main():
                         "ms": round(ms, 5), "busbw_fp32_equiv_GBs": round(bus_factor * n * 4 / (ms * 1e6), 2),
                         "algbw_GBs": round(n * 4 / (ms * 1e6), 2), "rel_err": float(rel_t.item()),
                         "ef": not args.no_ef and impl == "ours", "sr": not args.no_sr and impl != "nccl",
+                        **({"lag": lag} if lag is not None and len(args.lag) > 1 else {}),
                     }), flush=True)
         del x0, buf
     dist.barrier()

@@ -38,6 +38,7 @@ def main():
     p.add_argument("--sr", action="store_true")
     p.add_argument("--algo", default="twoshot")
     p.add_argument("--max-ctas", type=int, default=0)
+    p.add_argument("--lag", type=int, default=None, help="schedule lag of the fused kernel (-1 automatic, 0 phase-major)")
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=10)
     args = p.parse_args()
@@ -50,6 +51,8 @@ def main():
     comm = None
     if args.op in ("allreduce", "reduce_scatter", "all_gather"):
         comm = Communicator.create_local(0, workspace_bytes=max(256 << 20, 4 * args.n * args.bits // 8))
+        if args.lag is not None:
+            comm.set_schedule_lag(args.lag)
     packed = bitscom.compress_tensor(x, args.bits)
     out = torch.empty_like(x)
 

@@ -145,6 +145,10 @@ class Communicator:
         """Bound of every device-side wait on a peer flag."""
         self._c.set_timeout_ms(seconds * 1e3)
 
+    def set_schedule_lag(self, lag: int) -> None:
+        """Chunk-group lag of the kernel's work order: -1 automatic, 0 phase-major."""
+        self._c.set_schedule_lag(int(lag))
+
     def status(self) -> int:
         return int(self._c.status())
 

@@ -34,8 +34,9 @@ class LowBitHookState:
         stochastic_rounding: Philox stochastic rounding of the first quantisation.
         fp8: 8-bit buckets use the block-scaled E4M3 wire format.
         algo: "auto", "oneshot" or "twoshot".
-        max_ctas: CTAs of each fused launch (0 = one per SM); fewer leave SMs
-            to the overlapping backward kernels.
+        max_ctas: CTAs of each fused launch (0 = two per SM).  The default, 32,
+            leaves most SMs to the backward kernels the launch overlaps with
+            (ResNet-18 DDP on 8 B200s: 275K samples/s at 32 CTAs, 261K at 296).
         compress_single_rank: at world size 1 still run the (loopback) kernel,
             so a 1-GPU run applies exactly the quantisation an N-GPU run does.
         seed: Philox key of stochastic rounding.
@@ -49,7 +50,7 @@ class LowBitHookState:
         stochastic_rounding: bool = False,
         fp8: bool = False,
         algo: str = "auto",
-        max_ctas: int = 0,
+        max_ctas: int = 32,
         compress_single_rank: bool = True,
         seed: int = 0x5EED,
         use_comm_stream: bool = True,

@@ -253,6 +253,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "print the native stack on SIGSEGV/SIGABRT (debugging aid)");
   m.def("packed_bytes", [](int64_t n, int64_t bits) -> int64_t { return packed_bytes_ref(n, static_cast<int>(bits)); });
   m.def("wire_sub_bytes", [](int64_t bits) -> int64_t { return launch::coll_sub_bytes(static_cast<int>(bits)); });
+  m.def(
+      "coll_schedule",
+      [](int op, int world, int64_t items_per_slot, int64_t lag) {
+        int a1, a2, a3;
+        coll_phase_items(op, world, &a1, &a2, &a3);
+        const int64_t total = (a1 + a2 + a3) * items_per_slot;
+        std::vector<int64_t> order(static_cast<size_t>(total));
+        for (int64_t t = 0; t < total; ++t) order[t] = coll_schedule_item(op, world, items_per_slot, lag, t);
+        return order;
+      },
+      "Work item handed out for each ticket of a fused collective (the kernel's schedule, run on the host).",
+      py::arg("op"), py::arg("world"), py::arg("items_per_slot"), py::arg("lag"));
 
   py::class_<CollStats>(m, "CollStats")
       .def_readonly("calls", &CollStats::calls)
@@ -297,6 +309,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("status", &LowBitComm::status)
       .def("check", &LowBitComm::check)
       .def("set_timeout_ms", &LowBitComm::set_timeout_ms)
+      .def("set_schedule_lag", &LowBitComm::set_schedule_lag)
+      .def("schedule_lag", &LowBitComm::schedule_lag)
       .def_property_readonly("timeout_ms", &LowBitComm::timeout_ms)
       .def("set_fault_skip_signal", &LowBitComm::set_fault_skip_signal)
       .def("max_elems_per_launch", &LowBitComm::max_elems_per_launch)

@@ -4,6 +4,12 @@
 
 #include <stdint.h>
 
+#ifdef __CUDACC__
+#define BITSCOM_HD __host__ __device__
+#else
+#define BITSCOM_HD
+#endif
+
 namespace bitscom_b200 {
 
 constexpr int kMaxRanks = 8;          // one NVSwitch node
@@ -51,6 +57,7 @@ struct CollParams {
   int64_t n_sub;       // sub-chunks per slot (per shard; per tensor for one-shot)
   int sub_per_item;    // sub-chunks handled by one work item (one flag each)
   int64_t n_items_slot;  // items per slot = ceil(n_sub / sub_per_item)
+  int64_t lag;           // schedule lag in chunk groups (<= 0 or >= n_items_slot: phase-major order)
 
   const void* in;
   void* out;
@@ -79,5 +86,65 @@ struct CollParams {
   uint32_t* fault_skip; // test hook: when non-null and *fault_skip != 0 this rank skips its signals
   uint64_t timeout_ns;
 };
+
+// Work items per chunk in each phase of a collective (phase 1: encode and
+// push; phase 2: owner reduce; phase 3: decode a peer's reduced chunk).
+BITSCOM_HD inline void coll_phase_items(int op, int world, int* a1, int* a2, int* a3) {
+  switch (op) {
+    case kAllReduceTwoShot: *a1 = world; *a2 = 1; *a3 = world - 1; break;
+    case kReduceScatter:    *a1 = world; *a2 = 1; *a3 = 0; break;
+    case kAllReduceOneShot: *a1 = 1; *a2 = 1; *a3 = 0; break;
+    default:                *a1 = 1; *a2 = 0; *a3 = world - 1; break;  // all-gather
+  }
+}
+
+// Ticket -> work item.  Items are numbered phase-major: phase-1 item of chunk
+// c and destination k is c*a1 + k, phase-2 item of chunk c is n1 + c,
+// phase-3 item of chunk c and source k is n1 + n2 + c*a3 + k.  Tickets are
+// handed out in "groups": group g holds phase 1 of chunk g, phase 2 of chunk
+// g - lag and phase 3 of chunk g - 2*lag (g - lag when there is no phase 2),
+// so owners reduce and peers decode while later chunks are still being
+// encoded instead of after the whole phase 1.
+//
+// Deadlock freedom: every item waits only for items of a strictly earlier
+// group (phase 2 of chunk c for phase 1 of chunk c on every rank, phase 3
+// for phase 2 of chunk c on the owner), and every rank hands out tickets in
+// the same order.  The earliest unfinished ticket over all ranks therefore
+// waits for nothing unfinished, and it is claimed as soon as its rank has a
+// free CTA, which it has because every ticket that rank claimed before it is
+// finished.  This holds for any number of resident CTAs, so the kernel can
+// share the GPU with other work.
+BITSCOM_HD inline int64_t coll_schedule_item(int op, int world, int64_t IS, int64_t lag, int64_t t) {
+  int a1, a2, a3;
+  coll_phase_items(op, world, &a1, &a2, &a3);
+  const int64_t n1 = a1 * IS, n2 = a2 * IS, total = n1 + n2 + a3 * IS;
+  if (t >= total) return total;
+  if (lag <= 0 || lag >= IS) return t;
+  const int64_t L2 = lag;
+  const int64_t L3 = a2 ? 2 * lag : lag;
+  // Items handed out before group g.
+  auto before = [&](int64_t g) -> int64_t {
+    const int64_t p1 = g < IS ? g : IS;
+    const int64_t p2 = g - L2 < 0 ? 0 : (g - L2 < IS ? g - L2 : IS);
+    const int64_t p3 = g - L3 < 0 ? 0 : (g - L3 < IS ? g - L3 : IS);
+    return a1 * p1 + a2 * p2 + a3 * p3;
+  };
+  int64_t lo = 0, hi = IS + L3;  // before(lo) <= t < before(hi) == total
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (before(mid) <= t) lo = mid; else hi = mid;
+  }
+  const int64_t g = lo;
+  int64_t r = t - before(g);
+  if (g < IS) {
+    if (r < a1) return g * a1 + r;
+    r -= a1;
+  }
+  if (a2 != 0 && g >= L2 && g < IS + L2) {
+    if (r < a2) return n1 + (g - L2);
+    r -= a2;
+  }
+  return n1 + n2 + (g - L3) * a3 + r;
+}
 
 }  // namespace bitscom_b200

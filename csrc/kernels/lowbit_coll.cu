@@ -327,13 +327,9 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
   T* out = static_cast<T*>(p.out);
   const bool skip_signals = p.fault_skip != nullptr && *p.fault_skip != 0u;  // test hook
 
-  int64_t n1, n2, n3;
-  switch (p.op) {
-    case kAllReduceTwoShot: n1 = W * IS; n2 = IS; n3 = (W - 1) * IS; break;
-    case kReduceScatter:    n1 = W * IS; n2 = IS; n3 = 0; break;
-    case kAllReduceOneShot: n1 = IS; n2 = IS; n3 = 0; break;
-    default:                n1 = IS; n2 = 0; n3 = (W - 1) * IS; break;  // all-gather
-  }
+  int a1, a2, a3;
+  coll_phase_items(p.op, W, &a1, &a2, &a3);
+  const int64_t n1 = a1 * IS, n2 = a2 * IS, n3 = a3 * IS;
   const int64_t total = n1 + n2 + n3;
   const bool bcast1 = (p.op == kAllReduceOneShot || p.op == kAllGather);  // phase 1 stores to every rank
 
@@ -344,7 +340,8 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
   };
   auto grab = [&]() -> int64_t {
     const uint32_t t = atomicAdd(p.ticket, 1u);
-    return (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) ? total : static_cast<int64_t>(t);
+    if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) return total;
+    return coll_schedule_item(p.op, W, IS, p.lag, static_cast<int64_t>(t));
   };
 
   if (threadIdx.x == 0) s_item[0] = grab();

@@ -71,6 +71,7 @@ LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
   opened_[rank_] = true;
   if (world_ == 1) ready_ = true;
   if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) set_timeout_ms(std::atof(t));
+  if (const char* t = std::getenv("BITSCOM_SCHED_LAG")) sched_lag_ = std::atoll(t);
 }
 
 LowBitComm::~LowBitComm() {
@@ -215,16 +216,16 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   p.status = status_dev_;
   p.timeout_ns = timeout_ns_;
 
-  int64_t n1, n2, n3;
+  int a1, a2, a3;
+  coll_phase_items(op, world_, &a1, &a2, &a3);
   const int64_t IS = p.n_items_slot;
-  switch (op) {
-    case kAllReduceTwoShot: n1 = world_ * IS; n2 = IS; n3 = (world_ - 1) * IS; break;
-    case kReduceScatter: n1 = world_ * IS; n2 = IS; n3 = 0; break;
-    case kAllReduceOneShot: n1 = IS; n2 = IS; n3 = 0; break;
-    default: n1 = IS; n2 = 0; n3 = (world_ - 1) * IS; break;
-  }
-  const int64_t total = n1 + n2 + n3;
+  const int64_t total = (a1 + a2 + a3) * IS;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid_cap, total)));
+  // Schedule lag: phase 2 of a chunk is handed out `lag` groups after its
+  // phase 1.  About two waves of phase-1 items keeps the owner's wait short
+  // (the chunk's encodes have finished on every rank by then) while the
+  // reduce and decode work overlaps the encode stream.
+  p.lag = sched_lag_ >= 0 ? sched_lag_ : std::max<int64_t>(4, div_up(2 * static_cast<int64_t>(grid), a1));
   DeviceGuard g(device_);
   launch::lowbit_coll(p, dt, bits, grid, s);
   stats_.launches += 1;
@@ -245,9 +246,10 @@ void LowBitComm::allreduce(const void* in, void* out, float* residual, int64_t n
   int a = algo;
   if (a == kAlgoAuto) {
     // Small messages are latency bound: one launch-wide broadcast beats two
-    // dependent phases.  Threshold from the W=8 crossover of the two variants.
+    // dependent phases.  Measured crossover on B200 (4-bit, W=2 and W=8):
+    // one-shot wins up to 512 KB packed (4 MB fp32), two-shot from 1 MB.
     const int64_t packed = n * bits / 8;
-    a = (world_ == 1 || packed <= (world_ <= 2 ? (512ll << 10) : (128ll << 10))) ? kAlgoOneShot : kAlgoTwoShot;
+    a = (world_ == 1 || packed <= (512ll << 10)) ? kAlgoOneShot : kAlgoTwoShot;
   }
   const int op = (a == kAlgoOneShot) ? kAllReduceOneShot : kAllReduceTwoShot;
   const int64_t cap = max_elems_per_launch(op, bits);

@@ -78,6 +78,11 @@ class LowBitComm {
 
   void set_timeout_ms(double ms) { timeout_ns_ = static_cast<uint64_t>(ms * 1e6); }
   double timeout_ms() const { return static_cast<double>(timeout_ns_) / 1e6; }
+  // Chunk-group lag of the work schedule: -1 = automatic, 0 = phase-major
+  // (every encode before any reduce), k > 0 = reduce chunk c after encoding
+  // chunk c + k.  Env BITSCOM_SCHED_LAG sets the initial value.
+  void set_schedule_lag(int64_t lag) { sched_lag_ = lag < -1 ? -1 : lag; }
+  int64_t schedule_lag() const { return sched_lag_; }
   // Test hook: this rank stops storing its completion flags, so waiting peers time out.
   void set_fault_skip_signal(bool on);
   uint32_t epoch() const { return epoch_; }
@@ -109,6 +114,7 @@ class LowBitComm {
   int64_t data_off_ = 0, flag_off_ = 0, half_bytes_ = 0, flag_cap_ = 0;
   uint32_t epoch_ = 0;
   uint64_t timeout_ns_ = 100ull * 1000ull * 1000ull * 1000ull;  // 100 s default
+  int64_t sched_lag_ = -1;
   int sm_count_ = 148;
   bool ready_ = false;
   mutable bool broken_ = false;

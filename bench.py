@@ -61,6 +61,8 @@ def parse():
                    help="broadcast BatchNorm buffers from rank 0 before every forward (DDP's default); off by default "
                         "because the reference's training loop synchronises gradients only")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--eager", action="store_true",
+                   help="our arm: run the step eagerly instead of replaying it as one CUDA graph")
     p.add_argument("--ref-path", choices=["ef", "python"], default="ef",
                    help="reference arm: its C++ error-feedback backend path, or its Python LowBitGroup path")
     return p.parse_args()
@@ -111,7 +113,9 @@ def barrier_sync(world):
 
 def make_data(rank, batch, device):
     g = torch.Generator().manual_seed(0 + rank)
-    xs = torch.randn(POOL, batch, 3, 32, 32, generator=g)
+    # Images are stored NHWC (channels-last): the model sees x.permute(0, 3, 1, 2),
+    # a channels_last NCHW view, so no layout conversion runs per step.
+    xs = torch.randn(POOL, batch, 32, 32, 3, generator=g)
     ys = torch.randint(0, 10, (POOL, batch), generator=g)
     return xs, ys
 
@@ -128,10 +132,16 @@ def build_ours(args, rank, world, local):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local), **kw)
     torch.manual_seed(0)
     model = resnet18_cifar(10).cuda().to(memory_format=torch.channels_last)
-    ddp = nn.parallel.DistributedDataParallel(
-        model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True,
-        process_group=dist.group.WORLD,
-    )
+    # For whole-step graph capture DDP is built on a side stream (PyTorch's
+    # capture recipe for DDP); harmless in eager mode.
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ddp = nn.parallel.DistributedDataParallel(
+            model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True,
+            process_group=dist.group.WORLD,
+        )
+    torch.cuda.current_stream().wait_stream(side)
     if args.hook == "lowbit":
         extra = {} if args.max_ctas is None else {"max_ctas": args.max_ctas}
         state = bitscom.register_lowbit_hook(ddp, bitwidth=args.bits, error_feedback=True, algo=args.algo, **extra)
@@ -142,7 +152,7 @@ def build_ours(args, rank, world, local):
 
     def step(x, y):
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = F.cross_entropy(ddp(x), y)
+            loss = F.cross_entropy(ddp(x.permute(0, 3, 1, 2)), y)
         loss.backward()
         opt.step()
         opt.zero_grad(set_to_none=False)
@@ -229,7 +239,7 @@ def build_reference(args, rank, world, local):
 
     def step(x, y):
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = F.cross_entropy(model(x), y)
+            loss = F.cross_entropy(model(x.permute(0, 3, 1, 2)), y)
         loss.backward()
         sync_grads()
         opt.step()
@@ -242,12 +252,12 @@ def build_reference(args, rank, world, local):
 
 
 # ----------------------------------------------------------------------------
-def timed(step, xs_dev, ys_dev, steps, world, e2e_host=None):
+def timed(step, xs_dev, ys_dev, steps, world, e2e_host=None, bufs=None):
     """Device-timed K steps; with e2e_host=(xs_pinned, ys_pinned) each step
-    copies its batch H2D from pinned memory and reads the loss back D2H."""
+    copies its batch H2D from pinned memory (into `bufs`, e.g. a captured
+    graph's static inputs) and reads the loss back D2H."""
     loss_host = torch.empty(steps, dtype=torch.float32, pin_memory=True)
-    xbuf = torch.empty_like(xs_dev[0])
-    ybuf = torch.empty_like(ys_dev[0])
+    xbuf, ybuf = bufs if bufs is not None else (torch.empty_like(xs_dev[0]), torch.empty_like(ys_dev[0]))
     barrier_sync(world)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -257,10 +267,10 @@ def timed(step, xs_dev, ys_dev, steps, world, e2e_host=None):
         if e2e_host is not None:
             xbuf.copy_(e2e_host[0][j], non_blocking=True)
             ybuf.copy_(e2e_host[1][j], non_blocking=True)
-            loss = step(xbuf.contiguous(memory_format=torch.channels_last), ybuf)
+            loss = step(xbuf, ybuf)
             loss_host[i : i + 1].copy_(loss.detach().float().view(1), non_blocking=True)
         else:
-            step(xs_dev[j].contiguous(memory_format=torch.channels_last), ys_dev[j])
+            step(xs_dev[j], ys_dev[j])
     t1.record()
     barrier_sync(world)
     ms = t0.elapsed_time(t1)
@@ -288,8 +298,30 @@ def main():
     xs_dev, ys_dev = xs.cuda(), ys.cuda()
     xs_pin, ys_pin = xs.pin_memory(), ys.pin_memory()
 
+    graph = args.impl == "ours" and not args.eager and args.hook == "lowbit"
+    bufs = None
+    per_step_launches = None
+    if graph:
+        # Whole-step CUDA graph (forward, backward with the fused all-reduce
+        # launches of the DDP hook, optimizer): eager DDP warm-up on a side
+        # stream, then one capture.  Untimed.
+        from bitscom_b200.parallel.graphs import DDP_EAGER_WARMUP, GraphedStep
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(DDP_EAGER_WARMUP):
+                step(xs_dev[i % POOL], ys_dev[i % POOL])
+        torch.cuda.current_stream().wait_stream(side)
+        barrier_sync(world)
+        la = launches()
+        step = GraphedStep(step, [xs_dev[0], ys_dev[0]], warmup=0)
+        per_step_launches = launches() - la
+        bufs = tuple(step.static_inputs)
+        desc += ", whole step replayed as one CUDA graph"
+
     for i in range(args.warmup):
-        step(xs_dev[i % POOL].contiguous(memory_format=torch.channels_last), ys_dev[i % POOL])
+        step(xs_dev[i % POOL], ys_dev[i % POOL])
     barrier_sync(world)
 
     from bitscom_b200.utils.clocks import ClockSampler
@@ -298,10 +330,12 @@ def main():
     with ClockSampler(list(range(world)) if rank == 0 else [local]) as cs:
         ms, _ = timed(step, xs_dev, ys_dev, args.steps, world)
     l1 = launches()
+    if per_step_launches is not None:  # replays do not pass through the host
+        l1 = l0 + per_step_launches * args.steps
     ms = max_over_ranks(ms, world)
     e2e = None
     if not args.no_e2e:
-        ms_e2e, _ = timed(step, xs_dev, ys_dev, args.steps, world, e2e_host=(xs_pin, ys_pin))
+        ms_e2e, _ = timed(step, xs_dev, ys_dev, args.steps, world, e2e_host=(xs_pin, ys_pin), bufs=bufs)
         ms_e2e = max_over_ranks(ms_e2e, world)
         img_bytes = xs[0].numel() * xs.element_size() + ys[0].numel() * ys.element_size()
         e2e = {
@@ -342,6 +376,7 @@ def main():
                                 else "none (gradients only, as in the reference's loop)"),
                 "l2": f"rotating pool of {POOL} device-resident batches ({POOL * 3} MiB > 126 MiB L2)",
                 "implementation": desc,
+                "cuda_graph": graph,
             },
             "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"), "reasons": clocks.get("reasons")},
             "gpu_launches": int(l1 - l0),

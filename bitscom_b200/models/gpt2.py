@@ -90,7 +90,7 @@ class GPT2(nn.Module):
         logits = F.linear(self.ln_f(x), self.wte.weight)
         if targets is None:
             return logits
-        loss = F.cross_entropy(logits.float().view(-1, logits.size(-1)), targets.view(-1))
+        loss = F.cross_entropy(logits.float().reshape(-1, logits.size(-1)), targets.reshape(-1))
         return logits, loss
 
 

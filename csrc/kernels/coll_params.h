@@ -85,6 +85,13 @@ struct CollParams {
   uint32_t* status;     // host-mapped status word
   uint32_t* fault_skip; // test hook: when non-null and *fault_skip != 0 this rank skips its signals
   uint64_t timeout_ns;
+  // Device-side epoch.  When non-null the launch epoch is *epoch_ctr + 1
+  // (read by every CTA at start, stored back by the last CTA out) and
+  // `epoch` / `parity` above are ignored, so a launch replayed from a CUDA
+  // graph still gets a fresh epoch.  With offset_from_epoch the Philox call
+  // offset is `offset + epoch`, so replays draw fresh stochastic rounding.
+  uint32_t* epoch_ctr;
+  int offset_from_epoch;
 };
 
 // Work items per chunk in each phase of a collective (phase 1: encode and

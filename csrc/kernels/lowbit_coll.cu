@@ -145,30 +145,30 @@ __device__ __forceinline__ void put_scale(uint8_t* sub, int blk, float s) {
 // ---------------------------------------------------------------------------
 // Workspace addressing.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint8_t* rs_sub(const CollParams& p, int rank_base, int slot, int64_t sub) {
-  return p.peer_base[rank_base] + p.rs_data_off[p.parity] + (slot * p.slot_subs + sub) * p.sub_bytes;
+// `par` is the launch's epoch parity: consecutive launches alternate
+// between two sets of data regions and flag arrays.
+__device__ __forceinline__ uint8_t* rs_sub(const CollParams& p, int par, int rank_base, int slot, int64_t sub) {
+  return p.peer_base[rank_base] + p.rs_data_off[par] + (slot * p.slot_subs + sub) * p.sub_bytes;
 }
-__device__ __forceinline__ uint8_t* ag_sub(const CollParams& p, int rank_base, int slot, int64_t sub) {
-  return p.peer_base[rank_base] + p.ag_data_off[p.parity] + (slot * p.slot_subs + sub) * p.sub_bytes;
+__device__ __forceinline__ uint8_t* ag_sub(const CollParams& p, int par, int rank_base, int slot, int64_t sub) {
+  return p.peer_base[rank_base] + p.ag_data_off[par] + (slot * p.slot_subs + sub) * p.sub_bytes;
 }
-__device__ __forceinline__ uint32_t* rs_flag(const CollParams& p, int rank_base, int slot, int64_t item) {
-  return reinterpret_cast<uint32_t*>(p.peer_base[rank_base] + p.rs_flag_off[p.parity]) +
-         slot * p.slot_items + item;
+__device__ __forceinline__ uint32_t* rs_flag(const CollParams& p, int par, int rank_base, int slot, int64_t item) {
+  return reinterpret_cast<uint32_t*>(p.peer_base[rank_base] + p.rs_flag_off[par]) + slot * p.slot_items + item;
 }
-__device__ __forceinline__ uint32_t* ag_flag(const CollParams& p, int rank_base, int slot, int64_t item) {
-  return reinterpret_cast<uint32_t*>(p.peer_base[rank_base] + p.ag_flag_off[p.parity]) +
-         slot * p.slot_items + item;
+__device__ __forceinline__ uint32_t* ag_flag(const CollParams& p, int par, int rank_base, int slot, int64_t item) {
+  return reinterpret_cast<uint32_t*>(p.peer_base[rank_base] + p.ag_flag_off[par]) + slot * p.slot_items + item;
 }
 
 // ---------------------------------------------------------------------------
 // Bounded wait (one thread).  Returns false on timeout or launch abort.
 // ---------------------------------------------------------------------------
-__device__ bool wait_epoch(const CollParams& p, const uint32_t* flag) {
-  if (ld_acquire_sys(flag) == p.epoch) return true;
+__device__ bool wait_epoch(const CollParams& p, uint32_t epoch, const uint32_t* flag) {
+  if (ld_acquire_sys(flag) == epoch) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (ld_acquire_sys(flag) == p.epoch) return true;
+    if (ld_acquire_sys(flag) == epoch) return true;
     if ((++spins & 63u) == 0u) {
       if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) return false;
       if (globaltimer_ns() - t0 > p.timeout_ns) {
@@ -181,11 +181,6 @@ __device__ bool wait_epoch(const CollParams& p, const uint32_t* flag) {
     }
     __nanosleep(64);
   }
-}
-
-__device__ __forceinline__ void signal(const CollParams& p, uint32_t* flag) {
-  if (p.fault_skip != nullptr && *p.fault_skip != 0u) return;  // test hook: drop the signal
-  st_release_sys(flag, p.epoch);
 }
 
 // ---------------------------------------------------------------------------
@@ -302,6 +297,11 @@ __device__ __forceinline__ float encode_block(float (&v)[32], bool sr, uint64_t 
   return scale;
 }
 
+// Sources decoded per batch in the owner's reduce: about 16 payload words
+// per lane in flight (4 sources at 4 bits, 2 at 8 bits, 1 at 12/16 bits).
+template <int B>
+constexpr int kSrcBatch = (B <= 2) ? 8 : (16 / B > 0 ? 16 / B : 1);
+
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
@@ -313,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
   // after that write, which publishes it.
   __shared__ int64_t s_item[2];
   __shared__ int s_ok[2];
+  __shared__ uint32_t s_epoch;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -344,8 +345,20 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
     return coll_schedule_item(p.op, W, IS, p.lag, static_cast<int64_t>(t));
   };
 
-  if (threadIdx.x == 0) s_item[0] = grab();
+  if (threadIdx.x == 0) {
+    uint32_t e = p.epoch;
+    if (p.epoch_ctr != nullptr) {
+      // Every CTA reads the counter before the last CTA out advances it.
+      e = *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u;
+      if (e == 0u) e = 1u;  // 0 is the "never written" flag value
+    }
+    s_epoch = e;
+    s_item[0] = grab();
+  }
   __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int par = p.epoch_ctr != nullptr ? static_cast<int>(epoch & 1u) : p.parity;
+  const uint64_t offset = p.offset + (p.offset_from_epoch ? static_cast<uint64_t>(epoch) : 0ull);
   int cur = 0;
   while (true) {
     const int64_t item = s_item[cur];
@@ -377,20 +390,20 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
         float scale;
         if (has_res) {
           scale = encode_block<B, FMT, kKeepResidual>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
-                                                      1u + 4u * me, p.seed, p.offset, w);
+                                                      1u + 4u * me, p.seed, offset, w);
           store_block<float>(p.residual, base + off, base + lim, vr, lane, v);
         } else {
           scale = encode_block<B, FMT, kKeepInput>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
-                                                   1u + 4u * me, p.seed, p.offset, w);
+                                                   1u + 4u * me, p.seed, offset, w);
         }
         if (!bcast1) {
-          uint8_t* d = rs_sub(p, dst, me, sub);
+          uint8_t* d = rs_sub(p, par, dst, me, sub);
           put_words<B>(d, warp, lane, w);
           if (lane == 0) put_scale(d, warp, scale);
         } else {
           for (int k = 0; k < W; ++k) {
             const int d = (me + 1 + k) % W;
-            uint8_t* dp = (p.op == kAllGather) ? ag_sub(p, d, me, sub) : rs_sub(p, d, me, sub);
+            uint8_t* dp = (p.op == kAllGather) ? ag_sub(p, par, d, me, sub) : rs_sub(p, par, d, me, sub);
             put_words<B>(dp, warp, lane, w);
             if (lane == 0) put_scale(dp, warp, scale);
           }
@@ -407,10 +420,10 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
       // Completion flags, released by the last warp while the others move on.
       if (warp == kThreads / 32 - 1 && !skip_signals) {
         if (!bcast1) {
-          if (lane == 0) st_release_sys(rs_flag(p, dst, me, c), p.epoch);
+          if (lane == 0) st_release_sys(rs_flag(p, par, dst, me, c), epoch);
         } else if (lane < W) {
           const int d = (me + 1 + lane) % W;
-          st_release_sys((p.op == kAllGather) ? ag_flag(p, d, me, c) : rs_flag(p, d, me, c), p.epoch);
+          st_release_sys((p.op == kAllGather) ? ag_flag(p, par, d, me, c) : rs_flag(p, par, d, me, c), epoch);
         }
       }
     } else if (item < n1 + n2) {
@@ -418,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
       const int64_t c = item - n1;
       if (threadIdx.x == 0) {
         bool ok = true;
-        for (int s = 0; s < W && ok; ++s) ok = wait_epoch(p, rs_flag(p, me, s, c));
+        for (int s = 0; s < W && ok; ++s) ok = wait_epoch(p, epoch, rs_flag(p, par, me, s, c));
         s_ok[cur] = ok ? 1 : 0;
       }
       __syncthreads();
@@ -429,13 +442,28 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
         float acc[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-        for (int s = 0; s < W; ++s) {
-          const uint8_t* src = rs_sub(p, me, s, sub);
-          uint32_t w[B];
-          get_words<B>(src, warp, lane, w);
-          const float sc = get_scale(src, warp);
+        // Sources in batches of G: all G loads are in flight before the
+        // first decode, so a chunk costs ceil(W/G) memory latencies instead
+        // of W.  Sums stay in rank order (bit-identical on every rank).
+        constexpr int G = kSrcBatch<B>;
+        for (int s0 = 0; s0 < W; s0 += G) {
+          uint32_t wv[G][B];
+          float sc[G];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], C::decode(get_code<B>(w, j), sc));
+          for (int u = 0; u < G; ++u) {
+            if (s0 + u < W) {
+              const uint8_t* src = rs_sub(p, par, me, s0 + u, sub);
+              get_words<B>(src, warp, lane, wv[u]);
+              sc[u] = get_scale(src, warp);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < G; ++u) {
+            if (s0 + u < W) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], C::decode(get_code<B>(wv[u], j), sc[u]));
+            }
+          }
         }
         const int64_t off = sub * kSubElems + warp * kBlockElems;
         if (p.op == kAllReduceTwoShot) {
@@ -443,10 +471,10 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
           uint32_t w[B];
           const float scale = encode_block<B, FMT, kKeepDequant>(acc, p.stochastic2 != 0,
                                                                  static_cast<uint64_t>(elem_base >> 2) + lane,
-                                                                 2u + 4u * me, p.seed, p.offset, w);
+                                                                 2u + 4u * me, p.seed, offset, w);
           for (int k = 0; k < W; ++k) {
             const int d = (me + 1 + k) % W;
-            uint8_t* dp = ag_sub(p, d, me, sub);
+            uint8_t* dp = ag_sub(p, par, d, me, sub);
             put_words<B>(dp, warp, lane, w);
             if (lane == 0) put_scale(dp, warp, scale);
           }
@@ -465,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
         __syncthreads();
         if (warp == kThreads / 32 - 1 && lane < W && !skip_signals) {
           const int d = (me + 1 + lane) % W;
-          st_release_sys(ag_flag(p, d, me, c), p.epoch);
+          st_release_sys(ag_flag(p, par, d, me, c), epoch);
         }
       }
     } else {
@@ -473,19 +501,34 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
       const int64_t k3 = item - n1 - n2;
       const int64_t c = k3 / (W - 1);
       const int src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
-      if (threadIdx.x == 0) s_ok[cur] = wait_epoch(p, ag_flag(p, me, src, c)) ? 1 : 0;
+      if (threadIdx.x == 0) s_ok[cur] = wait_epoch(p, epoch, ag_flag(p, par, me, src, c)) ? 1 : 0;
       __syncthreads();
       if (!s_ok[cur]) break;
       const bool ag = p.op == kAllGather;
       const int64_t obase = ag ? static_cast<int64_t>(src) * p.out_stride : static_cast<int64_t>(src) * p.shard_len;
       const bool vo = vec_out && ((ag ? obase * static_cast<int64_t>(sizeof(T)) : 0) & 15) == 0;
+      // One sub-chunk of prefetch: the next sub-chunk's words are loaded
+      // before this one is decoded and stored.
+      const int64_t sub0 = c * p.sub_per_item;
+      uint32_t wn[B];
+      float scn = 0.0f;
+      if (sub0 < p.n_sub) {
+        const uint8_t* sp = ag_sub(p, par, me, src, sub0);
+        get_words<B>(sp, warp, lane, wn);
+        scn = get_scale(sp, warp);
+      }
       for (int g = 0; g < p.sub_per_item; ++g) {
-        const int64_t sub = c * p.sub_per_item + g;
+        const int64_t sub = sub0 + g;
         if (sub >= p.n_sub) break;
-        const uint8_t* sp = ag_sub(p, me, src, sub);
         uint32_t w[B];
-        get_words<B>(sp, warp, lane, w);
-        const float sc = get_scale(sp, warp);
+#pragma unroll
+        for (int q = 0; q < B; ++q) w[q] = wn[q];
+        const float sc = scn;
+        if (g + 1 < p.sub_per_item && sub + 1 < p.n_sub) {
+          const uint8_t* sp = ag_sub(p, par, me, src, sub + 1);
+          get_words<B>(sp, warp, lane, wn);
+          scn = get_scale(sp, warp);
+        }
         float o[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) o[j] = __fmul_rn(C::decode(get_code<B>(w, j), sc), p.post_scale);
@@ -503,6 +546,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
     __threadfence();
     const uint32_t prev = atomicAdd(p.done, 1u);
     if (prev == gridDim.x - 1) {
+      if (p.epoch_ctr != nullptr) *p.epoch_ctr = epoch;
       *p.ticket = 0u;
       *p.done = 0u;
       *p.abort_flag = 0u;

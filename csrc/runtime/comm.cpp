@@ -39,7 +39,7 @@ struct DeviceGuard {
 
 constexpr int64_t kCounterBytes = 4096;
 constexpr int64_t kMinSubBytes = kHeaderBytes + kSubBlocks * 128 * 1;  // 1-bit sub-chunk
-constexpr int kTicket = 0, kDone = 32, kAbort = 64, kFaultSkip = 96;  // word indices (128 B apart)
+constexpr int kTicket = 0, kDone = 32, kAbort = 64, kFaultSkip = 96, kEpoch = 128;  // word indices (128 B apart)
 
 int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -151,6 +151,13 @@ void LowBitComm::check() const {
   if (broken_) throw std::runtime_error("bitscom: communicator is broken by an earlier timeout; re-create it");
 }
 
+uint32_t LowBitComm::device_epoch() const {
+  DeviceGuard g(device_);
+  uint32_t v = 0;
+  ck(cudaMemcpy(&v, counters_ + kEpoch, 4, cudaMemcpyDeviceToHost), "device epoch");
+  return v;
+}
+
 void LowBitComm::set_fault_skip_signal(bool on) {
   DeviceGuard g(device_);
   const uint32_t v = on ? 1u : 0u;
@@ -213,6 +220,12 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   p.done = counters_ + kDone;
   p.abort_flag = counters_ + kAbort;
   p.fault_skip = counters_ + kFaultSkip;
+  // The launch epoch lives on the device, so a launch captured into a CUDA
+  // graph gets a fresh epoch (and, under capture, fresh stochastic-rounding
+  // draws) on every replay.
+  p.epoch_ctr = counters_ + kEpoch;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusActive) p.offset_from_epoch = 1;
   p.status = status_dev_;
   p.timeout_ns = timeout_ns_;
 
@@ -222,10 +235,11 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   const int64_t total = (a1 + a2 + a3) * IS;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid_cap, total)));
   // Schedule lag: phase 2 of a chunk is handed out `lag` groups after its
-  // phase 1.  About two waves of phase-1 items keeps the owner's wait short
-  // (the chunk's encodes have finished on every rank by then) while the
-  // reduce and decode work overlaps the encode stream.
-  p.lag = sched_lag_ >= 0 ? sched_lag_ : std::max<int64_t>(4, div_up(2 * static_cast<int64_t>(grid), a1));
+  // phase 1 (0 = phase-major).  Measured on B200 (4-bit EF, 16-512 MB): at
+  // W=1 and W=2 phase-major is fastest (a lag of two CTA waves is 3-9 %
+  // slower at W=2, a lag of 32 groups 60 % slower at W=1: owners then spin on
+  // chunks still being encoded), so automatic means phase-major.
+  p.lag = sched_lag_ >= 0 ? sched_lag_ : 0;
   DeviceGuard g(device_);
   launch::lowbit_coll(p, dt, bits, grid, s);
   stats_.launches += 1;

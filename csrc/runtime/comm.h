@@ -78,14 +78,18 @@ class LowBitComm {
 
   void set_timeout_ms(double ms) { timeout_ns_ = static_cast<uint64_t>(ms * 1e6); }
   double timeout_ms() const { return static_cast<double>(timeout_ns_) / 1e6; }
-  // Chunk-group lag of the work schedule: -1 = automatic, 0 = phase-major
-  // (every encode before any reduce), k > 0 = reduce chunk c after encoding
-  // chunk c + k.  Env BITSCOM_SCHED_LAG sets the initial value.
+  // Chunk-group lag of the work schedule: -1 = automatic (phase-major), 0 =
+  // phase-major (every encode before any reduce), k > 0 = reduce chunk c
+  // after encoding chunk c + k.  Env BITSCOM_SCHED_LAG sets the initial value.
   void set_schedule_lag(int64_t lag) { sched_lag_ = lag < -1 ? -1 : lag; }
   int64_t schedule_lag() const { return sched_lag_; }
   // Test hook: this rank stops storing its completion flags, so waiting peers time out.
   void set_fault_skip_signal(bool on);
+  // Launches issued from the host (replays of a captured launch advance only
+  // the device-side epoch).
   uint32_t epoch() const { return epoch_; }
+  // Epoch of the last completed launch as the device sees it (synchronising read).
+  uint32_t device_epoch() const;
   const CollStats& stats() const { return stats_; }
   void reset_stats() { stats_ = CollStats(); }
 

@@ -198,3 +198,68 @@ def test_sharded_dp_single_rank_trains(cuda):
     diff = (sdp.flat_param[lo : lo + sdp.shard] - sdp.master.detach()).abs().max()
     assert float(diff) < 0.02 * float(sdp.master.detach().abs().max())
     dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("algo", ["twoshot", "oneshot"])
+def test_graph_replay_matches_eager_and_advances_device_epoch(cuda, algo):
+    """A captured launch replayed K times equals K eager launches bit for bit
+    (error feedback carried across them) and advances the device-side epoch."""
+    n = 200003
+    xs = [_x(n, seed=40 + i) for i in range(4)]
+    ce = Communicator.create_local(0, workspace_bytes=64 << 20)
+    r_e = torch.zeros(n, device="cuda")
+    outs_e = []
+    for x in xs:
+        t = x.cuda()
+        ce.all_reduce(t, bits=4, algo=algo, residual=r_e, post_scale=0.5)
+        outs_e.append(t.clone())
+
+    c = Communicator.create_local(0, workspace_bytes=64 << 20)
+    c.set_timeout(5.0)
+    static = torch.zeros(n, device="cuda")
+    r_g = torch.zeros(n, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        c.all_reduce(static, bits=4, algo=algo, residual=r_g, post_scale=0.5)
+    torch.cuda.synchronize()
+    e0 = c.native.device_epoch()
+    outs_g = []
+    for x in xs:
+        static.copy_(x.cuda())
+        g.replay()
+        outs_g.append(static.clone())
+    torch.cuda.synchronize()
+    c.check()
+    assert c.native.device_epoch() == e0 + len(xs)
+    for a, b in zip(outs_e, outs_g):
+        assert torch.equal(a, b)
+    assert torch.equal(r_e, r_g)
+    # eager launches after the replays still find fresh epochs
+    t = xs[0].cuda()
+    c.all_reduce(t, bits=4, algo=algo)
+    torch.cuda.synchronize()
+    c.check()
+    assert c.native.device_epoch() == e0 + len(xs) + 1
+
+
+def test_graph_replays_draw_fresh_stochastic_rounding(cuda):
+    c = Communicator.create_local(0, workspace_bytes=64 << 20)
+    c.set_timeout(5.0)
+    x = torch.full((1 << 16,), 0.3, device="cuda")
+    x[::1024] = 1.0  # block absmax 1.0: 0.3 sits between two 2-bit codes
+    static = x.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        c.all_reduce(static, bits=2, algo="oneshot", stochastic_rounding=True, seed=3)
+    outs = []
+    for _ in range(2):
+        static.copy_(x)
+        g.replay()
+        outs.append(static.clone())
+    torch.cuda.synchronize()
+    c.check()
+    assert not torch.equal(outs[0], outs[1])
+    mask = torch.ones_like(x, dtype=torch.bool)
+    mask[::1024] = False
+    for o in outs:  # unbiased
+        assert abs(float(o[mask].mean()) - 0.3) < 0.01

@@ -285,3 +285,45 @@ def test_sharded_dp_replicas_identical():
     res = run_ranks(_w_sdp, 2, env=ENV, timeout=300)
     assert torch.equal(res[0][0], res[1][0])  # every rank decodes the same gathered bytes
     assert res[0][1][-1] < res[0][1][0]
+
+
+def _w_graph(rank, world):
+    from bitscom_b200.parallel.comm import Communicator
+
+    _init(rank, world)
+    comm = Communicator.for_group(None, rank)
+    comm.set_timeout(10.0)
+    n = 300001
+    xs = [_x(n, rank, seed=60 + i) for i in range(3)]
+    static = torch.zeros(n, device="cuda")
+    res = torch.zeros(n, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        comm.all_reduce(static, bits=4, algo="twoshot", residual=res, post_scale=1.0 / world)
+        comm.all_reduce(static, bits=8, algo="oneshot", post_scale=1.0)
+    outs = []
+    for x in xs:
+        static.copy_(x.cuda())
+        g.replay()
+        outs.append(static.cpu())
+    torch.cuda.synchronize()
+    comm.check()
+    del g
+    dist.destroy_process_group()
+    return xs, outs
+
+
+def test_graph_replay_across_ranks_matches_model():
+    """Two collectives captured in one CUDA graph and replayed three times on
+    every rank: the device-side epochs keep the ranks in step and error
+    feedback carries across replays."""
+    _need(2)
+    world = 2
+    res = run_ranks(_w_graph, world, env=ENV, timeout=300)
+    residuals = [torch.zeros(300001) for _ in range(world)]
+    for i in range(3):
+        inputs = [res[r][0][i] for r in range(world)]
+        mid, residuals = emu.allreduce_two_shot(inputs, 4, residuals=residuals, post_scale=1.0 / world)
+        exp, _ = emu.allreduce_one_shot([mid] * world, 8)
+        for r in range(world):
+            assert torch.equal(res[r][1][i], exp), (i, r)

@@ -70,6 +70,8 @@ def main():
     p.add_argument("--fp8", action="store_true", help="also run the E4M3 8-bit format")
     p.add_argument("--impls", nargs="+", default=["ours", "nccl"], choices=["ours", "nccl", "reference", "reference_ef"])
     p.add_argument("--no-ef", action="store_true")
+    p.add_argument("--residual-dtype", choices=["float32", "bfloat16"], default="float32",
+                   help="element type of our error-feedback residual")
     p.add_argument("--no-sr", action="store_true")
     p.add_argument("--algo", default="auto")
     p.add_argument("--warmup", type=int, default=5)
@@ -122,7 +124,7 @@ def main():
                 if impl == "nccl":
                     fn = lambda: dist.all_reduce(buf)
                 elif impl == "ours":
-                    res = None if args.no_ef else torch.zeros(n, device="cuda")
+                    res = None if args.no_ef else torch.zeros(n, device="cuda", dtype=getattr(torch, args.residual_dtype))
                     counter = [0]
 
                     def fn(res=res, bits=bits, fmt=fmt, counter=counter):
@@ -162,6 +164,7 @@ def main():
                         "ms": round(ms, 5), "busbw_fp32_equiv_GBs": round(bus_factor * n * 4 / (ms * 1e6), 2),
                         "algbw_GBs": round(n * 4 / (ms * 1e6), 2), "rel_err": float(rel_t.item()),
                         "ef": not args.no_ef and impl == "ours", "sr": not args.no_sr and impl != "nccl",
+                        **({"residual_dtype": args.residual_dtype} if impl == "ours" and not args.no_ef else {}),
                         **({"lag": lag} if lag is not None and len(args.lag) > 1 else {}),
                     }), flush=True)
         del x0, buf

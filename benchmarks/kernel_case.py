@@ -35,6 +35,7 @@ def main():
     p.add_argument("--fmt", default="int")
     p.add_argument("--dtype", default="float32")
     p.add_argument("--ef", action="store_true")
+    p.add_argument("--res-dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--sr", action="store_true")
     p.add_argument("--algo", default="twoshot")
     p.add_argument("--max-ctas", type=int, default=0)
@@ -47,7 +48,8 @@ def main():
     dt = getattr(torch, args.dtype)
     esz = torch.tensor([], dtype=dt).element_size()
     x = (torch.randn(args.n, device="cuda") * 1e-3).to(dt)
-    res = torch.zeros(args.n, device="cuda") if args.ef else None
+    res = torch.zeros(args.n, device="cuda", dtype=getattr(torch, args.res_dtype)) if args.ef else None
+    rsz = 4 if args.res_dtype == "float32" else 2
     comm = None
     if args.op in ("allreduce", "reduce_scatter", "all_gather"):
         comm = Communicator.create_local(0, workspace_bytes=max(256 << 20, 4 * args.n * args.bits // 8))
@@ -86,16 +88,16 @@ def main():
     packed_b = n * args.bits / 8
     if args.op == "allreduce":
         # read x (+ read/write residual) + write out, plus packed store+load of both phases
-        alg = n * esz * 2 + (8 * n if args.ef else 0) + 4 * packed_b
+        alg = n * esz * 2 + (2 * n * rsz if args.ef else 0) + 4 * packed_b
     elif args.op in ("reduce_scatter", "all_gather"):
-        alg = n * esz * 2 + (8 * n if args.ef else 0) + 2 * packed_b
+        alg = n * esz * 2 + (2 * n * rsz if args.ef else 0) + 2 * packed_b
     elif args.op == "compress":
         alg = 2 * n * esz + packed_b  # absmax pass + quantise pass + packed write
     elif args.op == "decompress":
         alg = packed_b + n * esz
     else:
-        alg = 3 * n * esz + (8 * n if args.ef else 0)
-    print(json.dumps({"op": args.op, "n": n, "bits": args.bits, "fmt": args.fmt, "dtype": args.dtype, "ef": args.ef,
+        alg = 3 * n * esz + (2 * n * rsz if args.ef else 0)
+    print(json.dumps({"op": args.op, "n": n, "bits": args.bits, "fmt": args.fmt, "dtype": args.dtype, "ef": args.ef, "res_dtype": args.res_dtype if args.ef else None,
                       "sr": args.sr, "algo": args.algo, "ms": round(ms, 5), "alg_bytes": int(alg),
                       "alg_GBs": round(alg / (ms * 1e6), 1)}))
 

@@ -179,8 +179,9 @@ class Communicator:
     ) -> torch.Tensor:
         """Low-bit SUM all-reduce (times ``post_scale``) in place or into ``out``.
 
-        ``residual`` (fp32, ``tensor.numel()`` elements) enables error feedback:
-        the kernel quantises ``tensor + residual`` and writes the new residual.
+        ``residual`` (fp32 or bf16, ``tensor.numel()`` elements) enables error
+        feedback: the kernel quantises ``tensor + residual`` and writes the new
+        residual.
         """
         self._c.allreduce(
             tensor, out, residual, bits, FMTS[fmt], ALGOS[algo], stochastic_rounding, stochastic_requant,

@@ -53,6 +53,8 @@ class LowBitShardedDP(nn.Module):
         stochastic_rounding: SR in the gradient reduce-scatter.
         use_fused: use the fused kernels (False: NCCL fp reduce-scatter /
             all-gather after a quantisation roundtrip, for comparison).
+        max_ctas: CTAs per fused launch (0 = two per SM).
+        residual_dtype: element type of the EF residuals (fp32 or bf16).
     """
 
     def __init__(
@@ -67,6 +69,7 @@ class LowBitShardedDP(nn.Module):
         stochastic_rounding: bool = False,
         use_fused: bool = True,
         max_ctas: int = 0,
+        residual_dtype: torch.dtype = torch.float32,
     ):
         super().__init__()
         self.module = module
@@ -108,8 +111,10 @@ class LowBitShardedDP(nn.Module):
         self.master = self.flat_param[lo : lo + self.shard].clone().requires_grad_(True)
         self.master.grad = torch.zeros_like(self.master)
         self.optimizer = optimizer_factory([self.master])
-        self.rs_residual = torch.zeros(total, dtype=torch.float32, device=dev) if error_feedback else None
-        self.ag_residual = torch.zeros(self.shard, dtype=torch.float32, device=dev) if error_feedback else None
+        if residual_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("residual_dtype must be torch.float32 or torch.bfloat16")
+        self.rs_residual = torch.zeros(total, dtype=residual_dtype, device=dev) if error_feedback else None
+        self.ag_residual = torch.zeros(self.shard, dtype=residual_dtype, device=dev) if error_feedback else None
         self.comm = None
         if use_fused and dev.type == "cuda":
             self.comm = (Communicator.create_local(dev.index) if self.world == 1

@@ -40,6 +40,8 @@ class LowBitHookState:
         compress_single_rank: at world size 1 still run the (loopback) kernel,
             so a 1-GPU run applies exactly the quantisation an N-GPU run does.
         seed: Philox key of stochastic rounding.
+        residual_dtype: element type of the EF residuals (torch.float32 or
+            torch.bfloat16; bf16 halves their HBM traffic inside the kernel).
     """
 
     def __init__(
@@ -54,6 +56,7 @@ class LowBitHookState:
         compress_single_rank: bool = True,
         seed: int = 0x5EED,
         use_comm_stream: bool = True,
+        residual_dtype: torch.dtype = torch.float32,
     ):
         if bitwidth not in (1, 2, 4, 8, 12, 16):
             raise ValueError(f"bitwidth must be one of (1, 2, 4, 8, 12, 16), got {bitwidth}")
@@ -67,6 +70,9 @@ class LowBitHookState:
         self.compress_single_rank = compress_single_rank
         self.seed = int(seed)
         self.use_comm_stream = use_comm_stream
+        if residual_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("residual_dtype must be torch.float32 or torch.bfloat16")
+        self.residual_dtype = residual_dtype
         self.calls = 0
         self.residuals: Dict[int, torch.Tensor] = {}
         self._comms: Dict[int, Optional[Communicator]] = {}
@@ -96,10 +102,10 @@ class LowBitHookState:
         if not self.error_feedback:
             return None
         r = self.residuals.get(bucket_index)
-        if r is not None and r.numel() == buf.numel() and r.device != buf.device:
-            r = self.residuals[bucket_index] = r.to(buf.device, torch.float32).contiguous()
+        if r is not None and r.numel() == buf.numel() and (r.device != buf.device or r.dtype != self.residual_dtype):
+            r = self.residuals[bucket_index] = r.to(buf.device, self.residual_dtype).contiguous()
         if r is None or r.numel() != buf.numel():
-            r = torch.zeros(buf.numel(), dtype=torch.float32, device=buf.device)
+            r = torch.zeros(buf.numel(), dtype=self.residual_dtype, device=buf.device)
             self.residuals[bucket_index] = r
         return r
 

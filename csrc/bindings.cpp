@@ -181,13 +181,14 @@ at::Tensor ef_roundtrip_op(const at::Tensor& x_in, const c10::optional<at::Tenso
 // ---------------------------------------------------------------------------
 // LowBitComm bindings
 // ---------------------------------------------------------------------------
-float* residual_ptr(const c10::optional<at::Tensor>& r, int64_t n, const at::Tensor& like) {
-  if (!r || !r->defined()) return nullptr;
-  TORCH_CHECK(r->is_cuda() && r->is_contiguous() && r->scalar_type() == at::kFloat,
-              "bitscom: residual must be a contiguous fp32 CUDA tensor");
+ResidualBuf residual_ptr(const c10::optional<at::Tensor>& r, int64_t n, const at::Tensor& like) {
+  if (!r || !r->defined()) return {};
+  TORCH_CHECK(r->is_cuda() && r->is_contiguous() &&
+                  (r->scalar_type() == at::kFloat || r->scalar_type() == at::kBFloat16),
+              "bitscom: residual must be a contiguous fp32 or bf16 CUDA tensor");
   TORCH_CHECK(r->numel() == n, "bitscom: residual has ", r->numel(), " elements, expected ", n);
   TORCH_CHECK(r->device() == like.device(), "bitscom: residual is on another device");
-  return r->data_ptr<float>();
+  return ResidualBuf(r->data_ptr(), r->scalar_type() == at::kFloat ? kF32 : kBF16);
 }
 
 void comm_allreduce(LowBitComm& c, at::Tensor& t, const c10::optional<at::Tensor>& out_opt,

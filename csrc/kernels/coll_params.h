@@ -61,7 +61,8 @@ struct CollParams {
 
   const void* in;
   void* out;
-  float* residual;     // error-feedback residual (fp32, same length as the quantised input) or null
+  void* residual;      // error-feedback residual (same length as the quantised input) or null
+  int res_dtype;       // residual element type: 0 = fp32, 1 = bf16 (DType values)
   float post_scale;    // outputs are multiplied by this (1/W for averaging)
   int stochastic;      // stochastic rounding of the first quantisation
   int stochastic2;     // stochastic rounding of the owner's requantisation

@@ -280,15 +280,22 @@ __device__ __forceinline__ float encode_block(float (&v)[32], bool sr, uint64_t 
   const float inv = 1.0f / scale;
 #pragma unroll
   for (int i = 0; i < B; ++i) w[i] = 0u;
+  // Stochastic rounding draws 16 bits per element: one Philox call (128
+  // bits) serves two float4 groups (k even: low halves, k odd: high halves),
+  // keyed by the even group's index.  16-bit uniforms bias a rounding by at
+  // most 2^-16 of a quantisation step and halve the generator's cost, which
+  // is the largest compute item of the encode.
+  Philox4 r{0u, 0u, 0u, 0u};
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    Philox4 r{0u, 0u, 0u, 0u};
-    if (FMT == kFmtInt && sr) r = sr_draws(grp0 + k * 32, stream, seed, offset);
+    if (FMT == kFmtInt && sr && (k & 1) == 0) r = sr_draws(grp0 + k * 32, stream, seed, offset);
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
       const int j = k * 4 + m;
       float deq;
-      const uint32_t code = C::encode(__fmul_rn(v[j], inv), sr, lane_of(r, m), scale, deq);
+      const uint32_t bits32 = lane_of(r, m);
+      const uint32_t draw = (k & 1) ? (bits32 & 0xFFFF0000u) : (bits32 << 16);  // 16 random bits on top
+      const uint32_t code = C::encode(__fmul_rn(v[j], inv), sr, draw, scale, deq);
       put_code<B>(w, j, code);
       if (KEEP == kKeepResidual) v[j] = __fsub_rn(v[j], deq);
       if (KEEP == kKeepDequant) v[j] = deq;
@@ -305,7 +312,7 @@ constexpr int kSrcBatch = (B <= 2) ? 8 : (16 / B > 0 ? 16 / B : 1);
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
-template <typename T, int B, int FMT>
+template <typename T, typename R, int B, int FMT>
 __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_constant__ CollParams p) {
   using C = Codec<B, FMT>;
   // Double-buffered by item parity: thread 0 writes the next slot while the
@@ -325,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
   const bool vec_res = (reinterpret_cast<uintptr_t>(p.residual) & 15u) == 0;
   const bool has_res = p.residual != nullptr;
   const T* in = static_cast<const T*>(p.in);
+  R* residual = static_cast<R*>(p.residual);
   T* out = static_cast<T*>(p.out);
   const bool skip_signals = p.fault_skip != nullptr && *p.fault_skip != 0u;  // test hook
 
@@ -373,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
       const int64_t base = bcast1 ? 0 : static_cast<int64_t>(dst) * p.in_stride;
       const int64_t lim = bcast1 ? p.n : shard_lim(dst);
       const bool vx = vec_in && ((base * static_cast<int64_t>(sizeof(T))) & 15) == 0;
-      const bool vr = vec_res && ((base * 4) & 15) == 0;
+      const bool vr = vec_res && ((base * static_cast<int64_t>(sizeof(R))) & 15) == 0;
       for (int g = 0; g < p.sub_per_item; ++g) {
         const int64_t sub = c * p.sub_per_item + g;
         if (sub >= p.n_sub) break;
@@ -382,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
         load_block<T>(in, base + off, base + lim, vx, lane, v);
         if (has_res) {
           float r[32];
-          load_block<float>(p.residual, base + off, base + lim, vr, lane, r);
+          load_block<R>(residual, base + off, base + lim, vr, lane, r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
         }
@@ -391,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
         if (has_res) {
           scale = encode_block<B, FMT, kKeepResidual>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
                                                       1u + 4u * me, p.seed, offset, w);
-          store_block<float>(p.residual, base + off, base + lim, vr, lane, v);
+          store_block<R>(residual, base + off, base + lim, vr, lane, v);
         } else {
           scale = encode_block<B, FMT, kKeepInput>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
                                                    1u + 4u * me, p.seed, offset, w);
@@ -573,6 +581,19 @@ void dispatch_bits_fmt(int bits, int fmt, F&& f) {
   }
 }
 
+template <int B, int F, typename T>
+void launch_res(const CollParams& p, int grid, cudaStream_t s) {
+  if (p.res_dtype == kBF16) lowbit_coll_kernel<T, __nv_bfloat16, B, F><<<grid, kThreads, 0, s>>>(p);
+  else lowbit_coll_kernel<T, float, B, F><<<grid, kThreads, 0, s>>>(p);
+}
+
+template <int B, int F>
+void launch_typed(const CollParams& p, DType dt, int grid, cudaStream_t s) {
+  if (dt == kF32) launch_res<B, F, float>(p, grid, s);
+  else if (dt == kBF16) launch_res<B, F, __nv_bfloat16>(p, grid, s);
+  else launch_res<B, F, __half>(p, grid, s);
+}
+
 }  // namespace
 
 namespace launch {
@@ -581,16 +602,9 @@ int64_t coll_sub_bytes(int bits) { return kHeaderBytes + static_cast<int64_t>(kS
 
 void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s) {
   if (p.world < 1 || p.world > kMaxRanks) throw std::runtime_error("bitscom: world size must be 1..8");
-  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) {
-    constexpr int B = decltype(bc)::value;
-    constexpr int F = decltype(fc)::value;
-    switch (dt) {
-      case kF32: lowbit_coll_kernel<float, B, F><<<grid, kThreads, 0, s>>>(p); break;
-      case kBF16: lowbit_coll_kernel<__nv_bfloat16, B, F><<<grid, kThreads, 0, s>>>(p); break;
-      case kF16: lowbit_coll_kernel<__half, B, F><<<grid, kThreads, 0, s>>>(p); break;
-      default: throw std::runtime_error("bitscom: unsupported dtype");
-    }
-  });
+  if (p.res_dtype != kF32 && p.res_dtype != kBF16) throw std::runtime_error("bitscom: residual must be fp32 or bf16");
+  if (dt != kF32 && dt != kBF16 && dt != kF16) throw std::runtime_error("bitscom: unsupported dtype");
+  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) { launch_typed<decltype(bc)::value, decltype(fc)::value>(p, dt, grid, s); });
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("lowbit_coll_kernel: ") + cudaGetErrorString(e));
 }
@@ -603,13 +617,8 @@ cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int gri
   if (p.fmt == kFmtE4M3 && bits != 8) return cudaErrorInvalidValue;
   if (bits != 1 && bits != 2 && bits != 4 && bits != 8 && bits != 12 && bits != 16) return cudaErrorInvalidValue;
   if (dt != kF32 && dt != kBF16 && dt != kF16) return cudaErrorInvalidValue;
-  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) {
-    constexpr int B = decltype(bc)::value;
-    constexpr int F = decltype(fc)::value;
-    if (dt == kF32) lowbit_coll_kernel<float, B, F><<<grid, kThreads, 0, s>>>(p);
-    else if (dt == kBF16) lowbit_coll_kernel<__nv_bfloat16, B, F><<<grid, kThreads, 0, s>>>(p);
-    else lowbit_coll_kernel<__half, B, F><<<grid, kThreads, 0, s>>>(p);
-  });
+  if (p.res_dtype != kF32 && p.res_dtype != kBF16) return cudaErrorInvalidValue;
+  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) { launch_typed<decltype(bc)::value, decltype(fc)::value>(p, dt, grid, s); });
   return cudaGetLastError();
 }
 

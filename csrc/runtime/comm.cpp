@@ -164,7 +164,7 @@ void LowBitComm::set_fault_skip_signal(bool on) {
   ck(cudaMemcpy(counters_ + kFaultSkip, &v, 4, cudaMemcpyHostToDevice), "fault skip");
 }
 
-void LowBitComm::launch(int op, const void* in, void* out, float* residual, int64_t n,
+void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual, int64_t n,
                         int64_t shard_len, int64_t in_stride, int64_t shard_valid, int64_t n_sub, DType dt, int bits, int fmt, bool sr,
                         bool sr2, uint64_t seed, uint64_t offset, float post_scale, cudaStream_t s,
                         int max_ctas, int64_t out_stride) {
@@ -200,7 +200,8 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   if (p.n_items_slot > L.slot_items) throw std::runtime_error("bitscom: flag capacity exceeded");
   p.in = in;
   p.out = out;
-  p.residual = residual;
+  p.residual = residual.ptr;
+  p.res_dtype = residual.dt;
   p.post_scale = post_scale;
   p.stochastic = sr ? 1 : 0;
   p.stochastic2 = sr2 ? 1 : 0;
@@ -249,7 +250,7 @@ void LowBitComm::launch(int op, const void* in, void* out, float* residual, int6
   else stats_.wire_bytes += static_cast<uint64_t>(world_ - 1) * n_sub * sub_b;
 }
 
-void LowBitComm::allreduce(const void* in, void* out, float* residual, int64_t n, DType dt, int bits,
+void LowBitComm::allreduce(const void* in, void* out, ResidualBuf residual, int64_t n, DType dt, int bits,
                            int fmt, int algo, bool sr, bool sr_requant, uint64_t seed, uint64_t offset,
                            float post_scale, cudaStream_t s, int max_ctas) {
   ensure_usable();
@@ -273,7 +274,7 @@ void LowBitComm::allreduce(const void* in, void* out, float* residual, int64_t n
     const int64_t m = std::min(seg, n - off);
     const char* ip = static_cast<const char*>(in) + off * esz;
     char* op_ = static_cast<char*>(out) + off * esz;
-    float* rp = residual ? residual + off : nullptr;
+    const ResidualBuf rp = residual.at(off);
     if (op == kAllReduceOneShot) {
       stats_.oneshot += 1;
       const int64_t n_sub = div_up(m, kSubElems);
@@ -289,7 +290,7 @@ void LowBitComm::allreduce(const void* in, void* out, float* residual, int64_t n
   }
 }
 
-void LowBitComm::reduce_scatter(const void* in, void* out, float* residual, int64_t shard, DType dt,
+void LowBitComm::reduce_scatter(const void* in, void* out, ResidualBuf residual, int64_t shard, DType dt,
                                 int bits, int fmt, bool sr, uint64_t seed, uint64_t offset,
                                 float post_scale, cudaStream_t s, int max_ctas) {
   ensure_usable();
@@ -305,13 +306,13 @@ void LowBitComm::reduce_scatter(const void* in, void* out, float* residual, int6
     const int64_t m = std::min(cap, shard - a);
     const int64_t m_pad = div_up(m, kSubElems) * kSubElems;
     launch(kReduceScatter, static_cast<const char*>(in) + a * esz, static_cast<char*>(out) + a * esz,
-           residual ? residual + a : nullptr, static_cast<int64_t>(world_ - 1) * shard + m, m_pad, shard, m,
+           residual.at(a), static_cast<int64_t>(world_ - 1) * shard + m, m_pad, shard, m,
            m_pad / kSubElems, dt, bits, fmt, sr, false, seed, offset + static_cast<uint64_t>(a), post_scale, s,
            max_ctas, 0);
   }
 }
 
-void LowBitComm::all_gather(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
+void LowBitComm::all_gather(const void* in, void* out, ResidualBuf residual, int64_t shard, DType dt, int bits,
                             int fmt, bool sr, uint64_t seed, uint64_t offset, cudaStream_t s,
                             int max_ctas) {
   ensure_usable();
@@ -327,7 +328,7 @@ void LowBitComm::all_gather(const void* in, void* out, float* residual, int64_t 
     const int64_t m = std::min(cap, shard - a);
     const int64_t n_sub = div_up(m, kSubElems);
     launch(kAllGather, static_cast<const char*>(in) + a * esz, static_cast<char*>(out) + a * esz,
-           residual ? residual + a : nullptr, m, n_sub * kSubElems, 0, m, n_sub, dt, bits, fmt, sr, false, seed,
+           residual.at(a), m, n_sub * kSubElems, 0, m, n_sub, dt, bits, fmt, sr, false, seed,
            offset + static_cast<uint64_t>(a), 1.0f, s, max_ctas, shard);
   }
 }

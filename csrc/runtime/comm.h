@@ -28,6 +28,23 @@ namespace bitscom_b200 {
 
 enum Algo : int { kAlgoAuto = 0, kAlgoTwoShot = 1, kAlgoOneShot = 2 };
 
+// Error-feedback residual: fp32 or bf16 elements (null = no error feedback).
+// A bf16 residual halves the residual's HBM traffic (read + write per
+// element); it rounds the stored error to 8 significant bits, i.e. to about
+// 1/500 of a quantisation step.
+struct ResidualBuf {
+  void* ptr = nullptr;
+  DType dt = kF32;
+  ResidualBuf() = default;
+  ResidualBuf(float* p) : ptr(p), dt(kF32) {}  // NOLINT: fp32 residuals convert implicitly
+  ResidualBuf(void* p, DType d) : ptr(p), dt(d) {}
+  explicit operator bool() const { return ptr != nullptr; }
+  ResidualBuf at(int64_t elems) const {
+    if (ptr == nullptr) return {};
+    return {static_cast<char*>(ptr) + elems * (dt == kF32 ? 4 : 2), dt};
+  }
+};
+
 struct CollStats {
   uint64_t calls = 0;
   uint64_t launches = 0;
@@ -56,16 +73,16 @@ class LowBitComm {
   bool ready() const { return ready_; }
 
   // All-reduce (SUM) of n elements: out = post_scale * sum_r dequant(quant(in_r + residual_r)).
-  // `residual` (fp32, n elements) is updated in place when non-null.
-  void allreduce(const void* in, void* out, float* residual, int64_t n, DType dt, int bits, int fmt,
+  // `residual` (fp32 or bf16, n elements) is updated in place when non-null.
+  void allreduce(const void* in, void* out, ResidualBuf residual, int64_t n, DType dt, int bits, int fmt,
                  int algo, bool sr, bool sr_requant, uint64_t seed, uint64_t offset,
                  float post_scale, cudaStream_t s, int max_ctas);
   // Reduce-scatter: `in` holds world*shard elements; this rank receives shard `rank` in `out`.
-  void reduce_scatter(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
+  void reduce_scatter(const void* in, void* out, ResidualBuf residual, int64_t shard, DType dt, int bits,
                       int fmt, bool sr, uint64_t seed, uint64_t offset, float post_scale,
                       cudaStream_t s, int max_ctas);
   // All-gather: `in` holds `shard` elements; `out` receives world*shard elements.
-  void all_gather(const void* in, void* out, float* residual, int64_t shard, DType dt, int bits,
+  void all_gather(const void* in, void* out, ResidualBuf residual, int64_t shard, DType dt, int bits,
                   int fmt, bool sr, uint64_t seed, uint64_t offset, cudaStream_t s, int max_ctas);
 
   // Host-mapped status of the launches so far (0 = ok).  Only meaningful once
@@ -102,7 +119,7 @@ class LowBitComm {
     int64_t rs_data[2], ag_data[2], rs_flag[2], ag_flag[2];
   };
   Layout layout(int bits) const;
-  void launch(int op, const void* in, void* out, float* residual, int64_t n, int64_t shard_len,
+  void launch(int op, const void* in, void* out, ResidualBuf residual, int64_t n, int64_t shard_len,
               int64_t in_stride, int64_t shard_valid, int64_t n_sub, DType dt, int bits, int fmt, bool sr, bool sr2, uint64_t seed,
               uint64_t offset, float post_scale, cudaStream_t s, int max_ctas, int64_t out_stride);
   void ensure_usable() const;

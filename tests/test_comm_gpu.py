@@ -263,3 +263,20 @@ def test_graph_replays_draw_fresh_stochastic_rounding(cuda):
     mask[::1024] = False
     for o in outs:  # unbiased
         assert abs(float(o[mask].mean()) - 0.3) < 0.01
+
+
+@pytest.mark.parametrize("algo", ["twoshot", "oneshot"])
+def test_allreduce_bf16_residual(comm, algo):
+    """bf16 error-feedback residual: read as bf16, summed in fp32, the new
+    residual rounded to bf16 (round to nearest even)."""
+    n = 123457
+    x = _x(n, seed=77)
+    r = (torch.randn(n) * 1e-4).to(torch.bfloat16)
+    t, rg = x.cuda(), r.cuda()
+    comm.all_reduce(t, bits=4, algo=algo, residual=rg)
+    torch.cuda.synchronize()
+    model = emu.allreduce_two_shot if algo == "twoshot" else emu.allreduce_one_shot
+    exp, res = model([x], 4, residuals=[r.float()])
+    assert torch.equal(t.cpu(), exp)
+    assert rg.dtype == torch.bfloat16
+    assert torch.equal(rg.cpu(), res[0].to(torch.bfloat16))

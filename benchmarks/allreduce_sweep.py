@@ -79,6 +79,8 @@ def main():
     p.add_argument("--max-ctas", type=int, default=0)
     p.add_argument("--lag", type=int, nargs="+", default=[-1],
                    help="schedule lags to sweep (-1 automatic, 0 phase-major)")
+    p.add_argument("--spi", type=int, nargs="+", default=[0],
+                   help="sub-chunks per work item to sweep (0 automatic)")
     args = p.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -116,10 +118,13 @@ def main():
         x0 = gradient_like(n, rank, "cuda")
         buf = x0.clone()
         bus_factor = 2.0 * (world - 1) / world if world > 1 else 1.0
-        runs = [(impl, lag) for impl in args.impls for lag in (args.lag if impl == "ours" else [None])]
-        for impl, lag in runs:
+        runs = [(impl, lag, spi) for impl in args.impls for lag in (args.lag if impl == "ours" else [None])
+                for spi in (args.spi if impl == "ours" else [None])]
+        for impl, lag, spi in runs:
             if lag is not None:
                 comm.set_schedule_lag(lag)
+            if spi is not None:
+                comm.set_sub_per_item(spi)
             for bits, fmt in formats if impl != "nccl" else [(32, "fp32")]:
                 if impl == "nccl":
                     fn = lambda: dist.all_reduce(buf)
@@ -166,6 +171,7 @@ def main():
                         "ef": not args.no_ef and impl == "ours", "sr": not args.no_sr and impl != "nccl",
                         **({"residual_dtype": args.residual_dtype} if impl == "ours" and not args.no_ef else {}),
                         **({"lag": lag} if lag is not None and len(args.lag) > 1 else {}),
+                        **({"spi": spi} if spi is not None and len(args.spi) > 1 else {}),
                     }), flush=True)
         del x0, buf
     dist.barrier()

@@ -149,6 +149,10 @@ class Communicator:
         """Chunk-group lag of the kernel's work order: -1 automatic, 0 phase-major."""
         self._c.set_schedule_lag(int(lag))
 
+    def set_sub_per_item(self, spi: int) -> None:
+        """Sub-chunks (8192 elements) per work item and completion flag: 0 automatic, 1..16 fixed."""
+        self._c.set_sub_per_item(int(spi))
+
     def status(self) -> int:
         return int(self._c.status())
 

@@ -160,11 +160,40 @@ class LowBitShardedDP(nn.Module):
         self.flat_grad.zero_()
 
     def state_dict_shard(self) -> dict:
-        """This rank's master shard, optimizer state and EF residuals."""
+        """This rank's master shard, its slice of the working parameters (the
+        values every rank decoded from the last low-bit all-gather), optimizer
+        state and EF residuals."""
+        lo = self.rank * self.shard
         return {
             "master": self.master.detach().cpu(),
+            "working": self.flat_param[lo : lo + self.shard].cpu(),
             "optimizer": self.optimizer.state_dict(),
             "rs_residual": None if self.rs_residual is None else self.rs_residual.cpu(),
             "ag_residual": None if self.ag_residual is None else self.ag_residual.cpu(),
             "calls": self._calls,
         }
+
+    @torch.no_grad()
+    def load_state_dict_shard(self, state: dict) -> None:
+        """Restore what :meth:`state_dict_shard` saved on this rank, then
+        all-gather the master shards into the working parameters (every rank
+        calls this, since the gather is collective)."""
+        master = state["master"]
+        if master.numel() != self.master.numel():
+            raise ValueError(f"checkpoint shard has {master.numel()} elements, this rank owns {self.master.numel()}")
+        self.master.copy_(master.to(self.master.device))
+        self.optimizer.load_state_dict(state["optimizer"])
+        for name in ("rs_residual", "ag_residual"):
+            mine, saved = getattr(self, name), state.get(name)
+            if mine is not None:
+                if saved is None:
+                    mine.zero_()
+                else:
+                    mine.copy_(saved.to(mine.device, mine.dtype))
+        self._calls = int(state.get("calls", 0))
+        # Working parameters: the saved decoded slices (exact resume), or the
+        # fp32 masters for a checkpoint without them.
+        work = state.get("working")
+        src = self.master.detach() if work is None else work.to(self.device, torch.float32)
+        dist.all_gather_into_tensor(self.flat_param, src.contiguous(), group=self.pg)
+        self.flat_grad.zero_()

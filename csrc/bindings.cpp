@@ -312,6 +312,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("set_timeout_ms", &LowBitComm::set_timeout_ms)
       .def("set_schedule_lag", &LowBitComm::set_schedule_lag)
       .def("device_epoch", &LowBitComm::device_epoch)
+      .def("set_sub_per_item", &LowBitComm::set_sub_per_item)
+      .def("sub_per_item", &LowBitComm::sub_per_item)
       .def("schedule_lag", &LowBitComm::schedule_lag)
       .def_property_readonly("timeout_ms", &LowBitComm::timeout_ms)
       .def("set_fault_skip_signal", &LowBitComm::set_fault_skip_signal)

@@ -72,6 +72,7 @@ LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
   if (world_ == 1) ready_ = true;
   if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) set_timeout_ms(std::atof(t));
   if (const char* t = std::getenv("BITSCOM_SCHED_LAG")) sched_lag_ = std::atoll(t);
+  if (const char* t = std::getenv("BITSCOM_SUB_PER_ITEM")) spi_override_ = std::atoi(t);
 }
 
 LowBitComm::~LowBitComm() {
@@ -194,6 +195,7 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   // fence is amortised over several sub-chunks, while small messages keep
   // one sub-chunk per item for parallelism.
   int64_t spi = div_up(phase1_units, 3 * static_cast<int64_t>(grid_cap));
+  if (spi_override_ > 0) spi = spi_override_;
   spi = std::max<int64_t>(1, std::min<int64_t>(16, spi));
   p.sub_per_item = static_cast<int>(spi);
   p.n_items_slot = div_up(n_sub, spi);

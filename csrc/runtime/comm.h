@@ -100,6 +100,11 @@ class LowBitComm {
   // after encoding chunk c + k.  Env BITSCOM_SCHED_LAG sets the initial value.
   void set_schedule_lag(int64_t lag) { sched_lag_ = lag < -1 ? -1 : lag; }
   int64_t schedule_lag() const { return sched_lag_; }
+  // Sub-chunks (8192 elements) per work item, i.e. per completion flag:
+  // 0 = automatic (about three phase-1 items per CTA), 1..16 = fixed.
+  // Env BITSCOM_SUB_PER_ITEM sets the initial value.
+  void set_sub_per_item(int spi) { spi_override_ = spi < 0 ? 0 : (spi > 16 ? 16 : spi); }
+  int sub_per_item() const { return spi_override_; }
   // Test hook: this rank stops storing its completion flags, so waiting peers time out.
   void set_fault_skip_signal(bool on);
   // Launches issued from the host (replays of a captured launch advance only
@@ -136,6 +141,7 @@ class LowBitComm {
   uint32_t epoch_ = 0;
   uint64_t timeout_ns_ = 100ull * 1000ull * 1000ull * 1000ull;  // 100 s default
   int64_t sched_lag_ = -1;
+  int spi_override_ = 0;
   int sm_count_ = 148;
   bool ready_ = false;
   mutable bool broken_ = false;

@@ -49,3 +49,31 @@ def test_ef_benefit_curve_cpu_shows_ef_gain():
 
     rows = ef_benefit_curve(torch.device("cpu"), 4, 40, 1 << 14, 0)
     assert rows[-1][2] < rows[-1][1] / 3  # EF cumulative error far below no-EF
+
+
+def test_graphed_step_rejects_bad_inputs():
+    import pytest
+    import torch
+
+    from bitscom_b200.parallel.graphs import GraphedStep
+
+    with pytest.raises(ValueError):
+        GraphedStep(lambda: None, [])
+    with pytest.raises(ValueError):
+        GraphedStep(lambda x: x, [torch.zeros(3)])  # CPU tensors cannot be captured
+
+
+def test_hook_state_residual_dtype():
+    import pytest
+    import torch
+
+    from bitscom_b200.parallel.hooks import LowBitHookState
+
+    s = LowBitHookState(residual_dtype=torch.bfloat16)
+    buf = torch.zeros(10)
+    r = s.residual(0, buf)
+    assert r.dtype == torch.bfloat16 and r.numel() == 10
+    s.residual_dtype = torch.float32
+    assert s.residual(0, buf).dtype == torch.float32  # converted on the next use
+    with pytest.raises(ValueError):
+        LowBitHookState(residual_dtype=torch.float16)

@@ -40,6 +40,7 @@ _EXTRA_DEFAULTS = {
     "max_ctas": 0,
     "seed": 0x5EED,
     "blocking_wait": False,
+    "oneshot_max_bytes": None,  # None: from the tuning table for this world size
 }
 _ALGOS = {"auto": 0, "twoshot": 1, "oneshot": 2}
 
@@ -64,6 +65,12 @@ def create_backend(store, rank: int, size: int, timeout, bitwidth: int = 4, erro
     opts.max_ctas = int(cfg["max_ctas"])
     opts.seed = int(cfg["seed"])
     opts.blocking_wait = bool(cfg["blocking_wait"])
+    if cfg["oneshot_max_bytes"] is None:
+        from .tuning import oneshot_max_bytes
+
+        opts.oneshot_max_bytes = oneshot_max_bytes(size)
+    else:
+        opts.oneshot_max_bytes = int(cfg["oneshot_max_bytes"])
 
     cpu_inner = dist.ProcessGroupGloo(dist.PrefixStore("lowbit_gloo/", store), rank, size, timeout)
     cuda_inner = None

@@ -52,6 +52,9 @@ class Communicator:
     def __init__(self, native, group=None):
         self._c = native
         self.group = group
+        from ..tuning import oneshot_max_bytes
+
+        native.set_oneshot_max_bytes(oneshot_max_bytes(native.world))
 
     # ------------------------------------------------------------------ setup
     @classmethod
@@ -152,6 +155,10 @@ class Communicator:
     def set_sub_per_item(self, spi: int) -> None:
         """Sub-chunks (8192 elements) per work item and completion flag: 0 automatic, 1..16 fixed."""
         self._c.set_sub_per_item(int(spi))
+
+    def check_canaries(self) -> int:
+        """Number of workspace guard regions that were overwritten (0 = none)."""
+        return int(self._c.check_canaries())
 
     def status(self) -> int:
         return int(self._c.status())

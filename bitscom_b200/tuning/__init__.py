@@ -1,0 +1,39 @@
+"""Tuning table of the fused collectives (algorithm crossover by world size).
+
+The table is a JSON file (``b200.json`` beside this module, or the file named
+by ``BITSCOM_TUNING_FILE``) with the largest packed message, in bytes per
+rank, for which the one-shot all-reduce is chosen automatically; larger
+messages use the two-shot form.  ``BITSCOM_ALGO=oneshot|twoshot`` overrides
+the automatic choice altogether (read by the native communicator).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from functools import lru_cache
+from typing import Optional
+
+_DEFAULT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "b200.json")
+FALLBACK_ONESHOT_MAX_BYTES = 512 << 10
+
+
+@lru_cache(maxsize=8)
+def load_table(path: Optional[str] = None) -> dict:
+    path = path or os.environ.get("BITSCOM_TUNING_FILE") or _DEFAULT
+    with open(path, encoding="utf-8") as fh:
+        table = json.load(fh)
+    if not isinstance(table, dict):
+        raise ValueError(f"tuning table {path} is not a JSON object")
+    return table
+
+
+def oneshot_max_bytes(world: int, path: Optional[str] = None) -> int:
+    """Automatic one-shot/two-shot threshold (packed bytes per rank) for `world` ranks."""
+    try:
+        table = load_table(path)
+    except (OSError, ValueError):
+        return FALLBACK_ONESHOT_MAX_BYTES
+    per_world = table.get("oneshot_max_packed_bytes", {})
+    v = per_world.get(str(int(world)), table.get("default_oneshot_max_packed_bytes", FALLBACK_ONESHOT_MAX_BYTES))
+    return int(v)

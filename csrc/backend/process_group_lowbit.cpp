@@ -224,6 +224,7 @@ std::shared_ptr<LowBitComm> ProcessGroupLowBit::comm(int device) {
     if (const char* mb = std::getenv("BITSCOM_WORKSPACE_MB")) ws = std::atoll(mb) << 20;
     c = std::make_shared<LowBitComm>(R, W, device, ws);
     c->set_timeout_ms(static_cast<double>(options_.timeout.count()));
+    c->set_oneshot_max_bytes(options_.oneshot_max_bytes);
     if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) c->set_timeout_ms(std::atof(t));
   } catch (const std::exception& e) {
     err = e.what();
@@ -712,6 +713,7 @@ void register_backend_bindings(pybind11::module& m) {
       .def_readwrite("algo", &LowBitOptions::algo)
       .def_readwrite("workspace_bytes", &LowBitOptions::workspace_bytes)
       .def_readwrite("max_ctas", &LowBitOptions::max_ctas)
+      .def_readwrite("oneshot_max_bytes", &LowBitOptions::oneshot_max_bytes)
       .def_readwrite("seed", &LowBitOptions::seed)
       .def_readwrite("blocking_wait", &LowBitOptions::blocking_wait);
 

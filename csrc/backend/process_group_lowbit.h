@@ -57,6 +57,7 @@ struct LowBitOptions {
   int max_ctas = 0;                  // 0 = one CTA per SM
   uint64_t seed = 0x5eed;
   bool blocking_wait = false;        // Work.wait() blocks the host and checks the kernel status
+  int64_t oneshot_max_bytes = 512ll << 10;  // automatic algorithm: one-shot up to this packed size
 };
 
 class WorkLowBit : public c10d::Work {

@@ -313,6 +313,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("set_schedule_lag", &LowBitComm::set_schedule_lag)
       .def("device_epoch", &LowBitComm::device_epoch)
       .def("set_sub_per_item", &LowBitComm::set_sub_per_item)
+      .def("set_oneshot_max_bytes", &LowBitComm::set_oneshot_max_bytes)
+      .def("oneshot_max_bytes", &LowBitComm::oneshot_max_bytes)
+      .def("check_canaries", &LowBitComm::check_canaries)
       .def("sub_per_item", &LowBitComm::sub_per_item)
       .def("schedule_lag", &LowBitComm::schedule_lag)
       .def_property_readonly("timeout_ms", &LowBitComm::timeout_ms)

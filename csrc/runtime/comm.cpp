@@ -40,6 +40,8 @@ struct DeviceGuard {
 constexpr int64_t kCounterBytes = 4096;
 constexpr int64_t kMinSubBytes = kHeaderBytes + kSubBlocks * 128 * 1;  // 1-bit sub-chunk
 constexpr int kTicket = 0, kDone = 32, kAbort = 64, kFaultSkip = 96, kEpoch = 128;  // word indices (128 B apart)
+constexpr int64_t kCanaryBytes = 256;
+constexpr int kCanaryByte = 0xA5;
 
 int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -57,10 +59,13 @@ LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
   half_bytes_ = ((workspace_bytes - kCounterBytes) * 95 / 100 / 4) & ~int64_t(4095);
   flag_cap_ = half_bytes_ / kMinSubBytes + 1;
   flag_off_ = kCounterBytes;
-  data_off_ = flag_off_ + ((4 * flag_cap_ * 4 + 4095) & ~int64_t(4095));
+  data_off_ = flag_off_ + ((4 * flag_cap_ * 4 + kCanaryBytes + 4095) & ~int64_t(4095));
   ws_bytes_ = data_off_ + 4 * half_bytes_;
   ck(cudaMalloc(&ws_, ws_bytes_), "cudaMalloc(workspace)");
   ck(cudaMemset(ws_, 0, data_off_), "cudaMemset(flags)");
+  // Guard bytes after the flag arrays and at the end of every data region
+  // (never addressed by a slot); check_canaries() reports any overwrite.
+  for (int64_t off : canary_offsets()) ck(cudaMemset(ws_ + off, kCanaryByte, kCanaryBytes), "cudaMemset(canary)");
   counters_ = reinterpret_cast<uint32_t*>(ws_);
   ck(cudaHostAlloc(&status_host_, 64, cudaHostAllocMapped | cudaHostAllocPortable), "cudaHostAlloc(status)");
   std::memset(status_host_, 0, 64);
@@ -73,6 +78,12 @@ LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
   if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) set_timeout_ms(std::atof(t));
   if (const char* t = std::getenv("BITSCOM_SCHED_LAG")) sched_lag_ = std::atoll(t);
   if (const char* t = std::getenv("BITSCOM_SUB_PER_ITEM")) spi_override_ = std::atoi(t);
+  if (const char* t = std::getenv("BITSCOM_ALGO")) {
+    const std::string a(t);
+    if (a == "oneshot") algo_override_ = kAlgoOneShot;
+    else if (a == "twoshot") algo_override_ = kAlgoTwoShot;
+    else if (a != "auto" && !a.empty()) throw std::runtime_error("bitscom: BITSCOM_ALGO must be auto, oneshot or twoshot");
+  }
 }
 
 LowBitComm::~LowBitComm() {
@@ -112,10 +123,34 @@ void LowBitComm::open_peers(const std::vector<std::vector<uint8_t>>& handles) {
   ready_ = true;
 }
 
+std::vector<int64_t> LowBitComm::canary_offsets() const {
+  std::vector<int64_t> v;
+  v.push_back(flag_off_ + 4 * flag_cap_ * 4);
+  for (int r = 0; r < 4; ++r) v.push_back(data_off_ + (r + 1) * half_bytes_ - kCanaryBytes);
+  return v;
+}
+
+int LowBitComm::check_canaries() const {
+  DeviceGuard g(device_);
+  ck(cudaDeviceSynchronize(), "canary sync");
+  std::vector<uint8_t> buf(kCanaryBytes);
+  int bad = 0;
+  for (int64_t off : canary_offsets()) {
+    ck(cudaMemcpy(buf.data(), ws_ + off, kCanaryBytes, cudaMemcpyDeviceToHost), "canary read");
+    for (uint8_t b : buf) {
+      if (b != static_cast<uint8_t>(kCanaryByte)) {
+        ++bad;
+        break;
+      }
+    }
+  }
+  return bad;
+}
+
 LowBitComm::Layout LowBitComm::layout(int bits) const {
   Layout L;
   L.sub_bytes = launch::coll_sub_bytes(bits);
-  L.slot_subs = half_bytes_ / (world_ * L.sub_bytes);
+  L.slot_subs = (half_bytes_ - kCanaryBytes) / (world_ * L.sub_bytes);
   L.slot_items = L.slot_subs;  // at most one flag per sub-chunk
   if (world_ * L.slot_items > flag_cap_) L.slot_items = flag_cap_ / world_;
   for (int p = 0; p < 2; ++p) {
@@ -260,13 +295,13 @@ void LowBitComm::allreduce(const void* in, void* out, ResidualBuf residual, int6
   const int esz = dt == kF32 ? 4 : 2;
   stats_.calls += 1;
   stats_.elements += static_cast<uint64_t>(n);
-  int a = algo;
+  int a = algo == kAlgoAuto ? algo_override_ : algo;
   if (a == kAlgoAuto) {
     // Small messages are latency bound: one launch-wide broadcast beats two
     // dependent phases.  Measured crossover on B200 (4-bit, W=2 and W=8):
     // one-shot wins up to 512 KB packed (4 MB fp32), two-shot from 1 MB.
     const int64_t packed = n * bits / 8;
-    a = (world_ == 1 || packed <= (512ll << 10)) ? kAlgoOneShot : kAlgoTwoShot;
+    a = (world_ == 1 || packed <= oneshot_max_bytes_) ? kAlgoOneShot : kAlgoTwoShot;
   }
   const int op = (a == kAlgoOneShot) ? kAllReduceOneShot : kAllReduceTwoShot;
   const int64_t cap = max_elems_per_launch(op, bits);

@@ -105,6 +105,15 @@ class LowBitComm {
   // Env BITSCOM_SUB_PER_ITEM sets the initial value.
   void set_sub_per_item(int spi) { spi_override_ = spi < 0 ? 0 : (spi > 16 ? 16 : spi); }
   int sub_per_item() const { return spi_override_; }
+  // Automatic algorithm choice: one-shot up to this many packed bytes per
+  // rank, two-shot above (tuning table; default 512 KB, the B200 crossover
+  // measured at W=2 and W=8).  Env BITSCOM_ALGO=oneshot|twoshot replaces the
+  // automatic choice.
+  void set_oneshot_max_bytes(int64_t b) { oneshot_max_bytes_ = b < 0 ? 0 : b; }
+  int64_t oneshot_max_bytes() const { return oneshot_max_bytes_; }
+  // Number of workspace guard regions whose bytes changed since creation
+  // (0 = none).  Synchronises the device.
+  int check_canaries() const;
   // Test hook: this rank stops storing its completion flags, so waiting peers time out.
   void set_fault_skip_signal(bool on);
   // Launches issued from the host (replays of a captured launch advance only
@@ -142,6 +151,9 @@ class LowBitComm {
   uint64_t timeout_ns_ = 100ull * 1000ull * 1000ull * 1000ull;  // 100 s default
   int64_t sched_lag_ = -1;
   int spi_override_ = 0;
+  int64_t oneshot_max_bytes_ = 512ll << 10;
+  int algo_override_ = kAlgoAuto;
+  std::vector<int64_t> canary_offsets() const;
   int sm_count_ = 148;
   bool ready_ = false;
   mutable bool broken_ = false;

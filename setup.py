@@ -41,6 +41,7 @@ setup(
     version="0.1.0",
     description="Blackwell-native low-bit gradient communication for PyTorch",
     packages=find_packages(include=["bitscom_b200", "bitscom_b200.*"]),
+    package_data={"bitscom_b200.tuning": ["*.json"]},
     ext_modules=[
         CUDAExtension(
             name="bitscom_b200._C",

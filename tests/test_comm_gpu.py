@@ -325,3 +325,14 @@ def test_sharded_dp_checkpoint_roundtrip(cuda):
         torch.testing.assert_close(b.master.detach(), a.master.detach(), rtol=1e-3, atol=1e-4)
     finally:
         dist.destroy_process_group()
+
+
+def test_workspace_guard_bytes_intact(comm):
+    """Runs after the other tests that share the module communicator: no
+    launch wrote into the guard bytes after the flag arrays or at the end of a
+    data region."""
+    x = torch.randn(comm.native.max_elems_per_launch(0, 1), device="cuda")  # the largest 1-bit two-shot launch
+    comm.all_reduce(x, bits=1, algo="twoshot")
+    comm.all_reduce(x[: 1 << 20], bits=16, algo="oneshot")
+    torch.cuda.synchronize()
+    assert comm.check_canaries() == 0

@@ -53,6 +53,7 @@ def _w_allreduce(rank, world, cases):
         torch.cuda.synchronize()
         comm.check()
         outs.append((x, r, t.cpu(), rg.cpu() if ef else None))
+    assert comm.check_canaries() == 0, "a launch wrote outside its workspace slots"
     dist.destroy_process_group()
     return outs
 

@@ -77,3 +77,23 @@ def test_hook_state_residual_dtype():
     assert s.residual(0, buf).dtype == torch.float32  # converted on the next use
     with pytest.raises(ValueError):
         LowBitHookState(residual_dtype=torch.float16)
+
+
+def test_tuning_table_thresholds(tmp_path, monkeypatch):
+    import json
+
+    from bitscom_b200 import tuning
+
+    tuning.load_table.cache_clear()
+    assert tuning.oneshot_max_bytes(8) == 524288  # shipped B200 table
+    assert tuning.oneshot_max_bytes(3) == tuning.load_table()["default_oneshot_max_packed_bytes"]
+    f = tmp_path / "t.json"
+    f.write_text(json.dumps({"oneshot_max_packed_bytes": {"2": 1234}, "default_oneshot_max_packed_bytes": 99}))
+    monkeypatch.setenv("BITSCOM_TUNING_FILE", str(f))
+    tuning.load_table.cache_clear()
+    assert tuning.oneshot_max_bytes(2) == 1234
+    assert tuning.oneshot_max_bytes(8) == 99
+    monkeypatch.setenv("BITSCOM_TUNING_FILE", str(tmp_path / "missing.json"))
+    tuning.load_table.cache_clear()
+    assert tuning.oneshot_max_bytes(2) == tuning.FALLBACK_ONESHOT_MAX_BYTES
+    tuning.load_table.cache_clear()

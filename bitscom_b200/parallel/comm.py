@@ -169,7 +169,12 @@ class Communicator:
 
     def stats(self) -> dict:
         s = self._c.stats()
-        return {k: getattr(s, k) for k in ("calls", "launches", "elements", "wire_bytes", "oneshot", "twoshot")}
+        keys = ("calls", "launches", "elements", "wire_bytes", "oneshot", "twoshot", "timed_launches", "kernel_ms")
+        return {k: getattr(s, k) for k in keys}
+
+    def set_timing(self, on: bool = True) -> None:
+        """Time every launch on the device (CUDA events); see ``stats()["kernel_ms"]``."""
+        self._c.set_timing(bool(on))
 
     # ------------------------------------------------------------ collectives
     def all_reduce(

@@ -38,6 +38,17 @@ from .comm import Communicator
 _ALIGN = 8192  # shard length granularity (one packed sub-chunk)
 
 
+def _cpu_copy(obj):
+    """Deep copy with every tensor cloned to host memory."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().to("cpu", copy=True)
+    if isinstance(obj, dict):
+        return {k: _cpu_copy(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_cpu_copy(v) for v in obj)
+    return obj
+
+
 class LowBitShardedDP(nn.Module):
     """Wraps ``module`` for sharded data-parallel training with low-bit
     reduce-scatter of gradients and low-bit all-gather of parameters.
@@ -167,7 +178,9 @@ class LowBitShardedDP(nn.Module):
         return {
             "master": self.master.detach().cpu(),
             "working": self.flat_param[lo : lo + self.shard].cpu(),
-            "optimizer": self.optimizer.state_dict(),
+            # a copy: the optimizer's state_dict() refers to the live state
+            # tensors, which later steps update in place
+            "optimizer": _cpu_copy(self.optimizer.state_dict()),
             "rs_residual": None if self.rs_residual is None else self.rs_residual.cpu(),
             "ag_residual": None if self.ag_residual is None else self.ag_residual.cpu(),
             "calls": self._calls,

@@ -273,7 +273,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readonly("elements", &CollStats::elements)
       .def_readonly("wire_bytes", &CollStats::wire_bytes)
       .def_readonly("oneshot", &CollStats::oneshot)
-      .def_readonly("twoshot", &CollStats::twoshot);
+      .def_readonly("twoshot", &CollStats::twoshot)
+      .def_readonly("timed_launches", &CollStats::timed_launches)
+      .def_readonly("kernel_ms", &CollStats::kernel_ms);
 
   py::class_<LowBitComm, std::shared_ptr<LowBitComm>>(m, "LowBitComm")
       .def(py::init<int, int, int, int64_t>(), py::arg("rank"), py::arg("world"), py::arg("device"),
@@ -321,7 +323,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("timeout_ms", &LowBitComm::timeout_ms)
       .def("set_fault_skip_signal", &LowBitComm::set_fault_skip_signal)
       .def("max_elems_per_launch", &LowBitComm::max_elems_per_launch)
-      .def("stats", &LowBitComm::stats, py::return_value_policy::copy)
+      .def("stats", &LowBitComm::stats)
+      .def("set_timing", &LowBitComm::set_timing)
+      .def_property_readonly("timing", &LowBitComm::timing)
       .def("reset_stats", &LowBitComm::reset_stats);
 
   register_backend_bindings(m);

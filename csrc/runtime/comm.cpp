@@ -91,6 +91,11 @@ LowBitComm::~LowBitComm() {
   cudaGetDevice(&cur);
   cudaSetDevice(device_);
   cudaDeviceSynchronize();
+  for (auto& pr : timed_) {
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
+  for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
   for (int r = 0; r < world_; ++r)
     if (r != rank_ && opened_[r] && peers_[r]) cudaIpcCloseMemHandle(peers_[r]);
   if (ws_) cudaFree(ws_);
@@ -121,6 +126,49 @@ void LowBitComm::open_peers(const std::vector<std::vector<uint8_t>>& handles) {
     opened_[r] = true;
   }
   ready_ = true;
+}
+
+cudaEvent_t LowBitComm::take_event() {
+  if (!event_pool_.empty()) {
+    cudaEvent_t e = event_pool_.back();
+    event_pool_.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  ck(cudaEventCreate(&e), "cudaEventCreate");
+  return e;
+}
+
+void LowBitComm::collect_timings(bool wait) {
+  DeviceGuard g(device_);
+  size_t keep = 0;
+  for (size_t i = 0; i < timed_.size(); ++i) {
+    auto pr = timed_[i];
+    if (wait) cudaEventSynchronize(pr.second);
+    if (cudaEventQuery(pr.second) == cudaSuccess) {
+      float ms = 0.0f;
+      if (cudaEventElapsedTime(&ms, pr.first, pr.second) == cudaSuccess) {
+        stats_.kernel_ms += ms;
+        stats_.timed_launches += 1;
+      }
+      event_pool_.push_back(pr.first);
+      event_pool_.push_back(pr.second);
+    } else {
+      timed_[keep++] = pr;
+    }
+  }
+  timed_.resize(keep);
+  cudaGetLastError();  // a not-ready query leaves cudaErrorNotReady behind
+}
+
+CollStats LowBitComm::stats() {
+  collect_timings(false);
+  return stats_;
+}
+
+void LowBitComm::reset_stats() {
+  collect_timings(true);
+  stats_ = CollStats();
 }
 
 std::vector<int64_t> LowBitComm::canary_offsets() const {
@@ -279,7 +327,19 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   // chunks still being encoded), so automatic means phase-major.
   p.lag = sched_lag_ >= 0 ? sched_lag_ : 0;
   DeviceGuard g(device_);
+  const bool timed = timing_ && !p.offset_from_epoch;  // never under capture
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (timed) {
+    e0 = take_event();
+    e1 = take_event();
+    ck(cudaEventRecord(e0, s), "cudaEventRecord");
+  }
   launch::lowbit_coll(p, dt, bits, grid, s);
+  if (timed) {
+    ck(cudaEventRecord(e1, s), "cudaEventRecord");
+    timed_.emplace_back(e0, e1);
+    if (timed_.size() > 4096) collect_timings(true);  // bound the in-flight list
+  }
   stats_.launches += 1;
   const int64_t sub_b = L.sub_bytes;
   if (op == kAllReduceTwoShot) stats_.wire_bytes += 2ull * (world_ - 1) * n_sub * sub_b;

@@ -52,6 +52,8 @@ struct CollStats {
   uint64_t wire_bytes = 0;  // packed bytes this rank stored to peers
   uint64_t oneshot = 0;
   uint64_t twoshot = 0;
+  uint64_t timed_launches = 0;  // launches whose device time is in kernel_ms
+  double kernel_ms = 0.0;       // summed device time of timed launches (set_timing)
 };
 
 class LowBitComm {
@@ -121,8 +123,14 @@ class LowBitComm {
   uint32_t epoch() const { return epoch_; }
   // Epoch of the last completed launch as the device sees it (synchronising read).
   uint32_t device_epoch() const;
-  const CollStats& stats() const { return stats_; }
-  void reset_stats() { stats_ = CollStats(); }
+  // Counters; folds in the device time of every timed launch that has
+  // completed (launches still running are added by a later call).
+  CollStats stats();
+  void reset_stats();
+  // Time every launch with a pair of CUDA events on its stream (off by
+  // default; launches under stream capture are never timed).
+  void set_timing(bool on) { timing_ = on; }
+  bool timing() const { return timing_; }
 
   // Segment capacity in elements for an op (for tests and planning).
   int64_t max_elems_per_launch(int op, int bits) const;
@@ -158,6 +166,11 @@ class LowBitComm {
   bool ready_ = false;
   mutable bool broken_ = false;
   CollStats stats_;
+  bool timing_ = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;  // in flight
+  std::vector<cudaEvent_t> event_pool_;
+  cudaEvent_t take_event();
+  void collect_timings(bool wait);
 };
 
 }  // namespace bitscom_b200

@@ -336,3 +336,19 @@ def test_workspace_guard_bytes_intact(comm):
     comm.all_reduce(x[: 1 << 20], bits=16, algo="oneshot")
     torch.cuda.synchronize()
     assert comm.check_canaries() == 0
+
+
+def test_launch_timing_in_stats(cuda):
+    c = Communicator.create_local(0, workspace_bytes=64 << 20)
+    c.set_timing(True)
+    t = torch.randn(1 << 20, device="cuda")
+    for _ in range(3):
+        c.all_reduce(t, bits=4, algo="twoshot")
+    torch.cuda.synchronize()
+    s = c.stats()
+    assert s["launches"] == 3 and s["timed_launches"] == 3
+    assert s["kernel_ms"] > 0.0
+    c.set_timing(False)
+    c.all_reduce(t, bits=4)
+    torch.cuda.synchronize()
+    assert c.stats()["timed_launches"] == 3

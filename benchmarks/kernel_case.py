@@ -28,7 +28,8 @@ from bitscom_b200.parallel.comm import Communicator  # noqa: E402
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--op", choices=["allreduce", "reduce_scatter", "all_gather", "compress", "decompress", "ef_roundtrip"],
+    p.add_argument("--op", choices=["allreduce", "reduce_scatter", "all_gather", "compress", "decompress", "ef_roundtrip",
+                                    "standalone"],
                    default="allreduce")
     p.add_argument("--n", type=int, default=1 << 26)
     p.add_argument("--bits", type=int, default=4)
@@ -56,6 +57,7 @@ def main():
         if args.lag is not None:
             comm.set_schedule_lag(args.lag)
     packed = bitscom.compress_tensor(x, args.bits)
+    res_sa = torch.zeros(args.n, device="cuda") if args.op == "standalone" else None
     out = torch.empty_like(x)
 
     def call():
@@ -70,6 +72,18 @@ def main():
             bitscom.compress_tensor(x, args.bits, stochastic_rounding=args.sr)
         elif args.op == "decompress":
             bitscom.decompress_tensor(packed)
+        elif args.op == "standalone":
+            # every standalone kernel once: absmax + quantise (int16), pack,
+            # unpack, int16 dequantise, fused compress, fused decompress, EF roundtrip
+            from bitscom_b200.quantization import dequantize_tensor, pack_lowbit, quantize_tensor, unpack_lowbit
+
+            q, scale = quantize_tensor(x, args.bits)
+            pk, _ = pack_lowbit(q, args.bits)
+            q2 = unpack_lowbit(pk, args.bits, x.numel())
+            dequantize_tensor(q2, scale, dtype=x.dtype, shape=x.shape)
+            bitscom.compress_tensor(x, args.bits)
+            bitscom.decompress_tensor(packed)
+            bitscom.ef_roundtrip(x, res_sa, args.bits)
         else:
             bitscom.ef_roundtrip(x, res, args.bits, stochastic_rounding=args.sr)
 
@@ -95,6 +109,8 @@ def main():
         alg = 2 * n * esz + packed_b  # absmax pass + quantise pass + packed write
     elif args.op == "decompress":
         alg = packed_b + n * esz
+    elif args.op == "standalone":
+        alg = 0  # a mix of kernels: only the per-kernel profile is meaningful
     else:
         alg = 3 * n * esz + (2 * n * rsz if args.ef else 0)
     print(json.dumps({"op": args.op, "n": n, "bits": args.bits, "fmt": args.fmt, "dtype": args.dtype, "ef": args.ef, "res_dtype": args.res_dtype if args.ef else None,

@@ -20,12 +20,14 @@
 //   reduce-scatter       phases 1+2, fp output shard.
 //   all-gather           quantise own shard once, broadcast, unpack all shards.
 //
-// Work distribution is a per-launch ticket counter: CTAs claim items in
-// phase order (all phase-1 items are claimed before any phase-2 item, ...).
-// Phase-1 items never wait, so every wait depends only on items that have
-// already been claimed by running CTAs; the kernel therefore cannot deadlock
-// even when only part of its grid is resident (e.g. sharing SMs with backward
-// kernels), which a static CTA->chunk mapping would not guarantee.
+// Work distribution is a per-launch ticket counter mapped to items by
+// coll_schedule_item (coll_params.h): phase order by default (all phase-1
+// items are handed out before any phase-2 item, ...), or phases interleaved
+// with a lag.  Every item waits only for items handed out earlier on every
+// rank, so every wait depends on items already claimed by running CTAs; the
+// kernel therefore cannot deadlock even when only part of its grid is
+// resident (e.g. sharing SMs with backward kernels), which a static
+// CTA->chunk mapping would not guarantee.
 //
 // Every wait is bounded by %globaltimer: on expiry the CTA records
 // kStatusTimeout in a host-mapped status word, raises a launch-local abort

@@ -133,3 +133,31 @@ def test_kernels_run_on_current_stream(cuda):
         y = decompress_tensor(c)
     s.synchronize()
     assert torch.equal(y.cpu(), decompress_tensor(compress_tensor(x.cpu(), 4)))
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8, 12, 16])
+@pytest.mark.parametrize("amax", [7.0, 0.7, 3.0e-3, 12345.678])
+def test_quantize_near_ties_matches_cpu(cuda, bits, amax):
+    """Values whose quotient x / scale sits on, or one or two ulps around, a
+    half-integer: the kernel must round the correctly rounded fp32 quotient
+    half-to-even, exactly as the reference's CPU code does."""
+    from bitscom_b200.quantization import _quant_bounds
+
+    _, qmax = _quant_bounds(bits)
+    scale = torch.tensor(amax / qmax, dtype=torch.float64).float()
+    k = torch.arange(-qmax, qmax, dtype=torch.float32)
+    mid = (k + 0.5) * scale
+    vals = [mid]
+    for d in (1, 2):
+        up, dn = mid.clone(), mid.clone()
+        for _ in range(d):
+            up = torch.nextafter(up, torch.full_like(up, float("inf")))
+            dn = torch.nextafter(dn, torch.full_like(dn, -float("inf")))
+        vals += [up, dn]
+    x = torch.cat(vals + [torch.tensor([amax, -amax])]).clamp(-amax, amax)
+    q_cpu, s_cpu = quantize_tensor(x, bits)
+    q_gpu, s_gpu = quantize_tensor(x.to(cuda), bits)
+    assert s_gpu == s_cpu
+    assert torch.equal(q_gpu.cpu(), q_cpu)
+    c_cpu, c_gpu = compress_tensor(x, bits), compress_tensor(x.to(cuda), bits)
+    assert torch.equal(c_gpu.packed.cpu(), c_cpu.packed)

@@ -18,6 +18,8 @@ DDP::
 from .api import LowBitGroup
 from .lowbit_backend import backend_options, is_extension_available, register_lowbit_backend
 from .parallel.comm import Communicator
+from .parallel.fsdp import LowBitShardedDP
+from .parallel.graphs import GraphedStep
 from .parallel.hooks import LowBitHookState, lowbit_allreduce_hook, register_lowbit_hook
 from .quantization import (
     SUPPORTED_BITWIDTHS,
@@ -45,6 +47,8 @@ __all__ = [
     "LowBitHookState",
     "lowbit_allreduce_hook",
     "register_lowbit_hook",
+    "LowBitShardedDP",
+    "GraphedStep",
     "CompressedTensor",
     "compress_tensor",
     "decompress_tensor",

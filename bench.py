@@ -38,7 +38,7 @@ import torch.nn.functional as F
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "DDP samples/s (ResNet-18 CIFAR, 4-bit EF low-bit all-reduce)"
-BASELINE_VALUE = None  # the reference publishes no ResNet-18 DDP number (BASELINE.md)
+BASELINE_VALUE = None  # the reference publishes no ResNet-18 DDP number
 L2_BYTES = 126 * 2**20
 POOL = 48  # distinct input batches cycled through (48 x 3 MiB > L2)
 

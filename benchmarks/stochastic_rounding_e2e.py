@@ -3,11 +3,14 @@ all-reduce without SR, with SR, and without compression.
 
 Counterpart of reference benchmarks/stochastic_rounding_e2e_curve.py
 (published: benchmarks/outputs/e2e_loss_curve_stochastic_vs_nocompress_bw4.csv).
-TinyMLP 256-512-512-10, teacher-labelled synthetic data (a fixed random
-teacher network labels N(0,1) inputs), per-parameter LowBitGroup.all_reduce
-and division by the world size, SGD momentum 0.9, gradient clipping 1.0.
-The "no compression" run here is a real fp32 all-reduce (the reference's was
-secretly its 4-bit C++ path).
+Same workload as that script, so the curves compare: TinyMLP 256-512-512-10;
+each rank owns a fixed dataset of 8192 N(0,1) inputs (generator seed
+data_seed + 100000 * rank) labelled by the argmax of one linear teacher shared
+by all ranks (seed data_seed + 9999); batches of 128 are read sequentially
+with wrap-around; per-parameter LowBitGroup.all_reduce and division by the
+world size; SGD momentum 0.9, lr 0.05, gradient clipping 1.0.  The "no
+compression" run here is a real fp32 all-reduce (the reference's ran its
+4-bit C++ path).
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
         benchmarks/stochastic_rounding_e2e.py --bitwidth 4 --steps 160 --out curve.csv
@@ -31,20 +34,34 @@ from bitscom_b200 import LowBitGroup  # noqa: E402
 from bitscom_b200.models import tiny_mlp_sr  # noqa: E402
 
 
+def local_dataset(args, rank):
+    """Fixed per-rank inputs labelled by a linear teacher common to all ranks."""
+    g = torch.Generator(device="cpu").manual_seed(args.data_seed + 100_000 * rank)
+    tg = torch.Generator(device="cpu").manual_seed(args.data_seed + 9999)
+    x = torch.randn(args.dataset_size, 256, generator=g)
+    w = torch.randn(256, 10, generator=tg)
+    b = torch.randn(10, generator=tg)
+    return x, torch.argmax(x @ w + b, dim=1)
+
+
+def batch_at(step, args, data, device):
+    x, y = data
+    n = x.size(0)
+    idx = (torch.arange(args.batch) + (step * args.batch) % n) % n
+    return x[idx].to(device), y[idx].to(device)
+
+
 def run(mode, args, rank, world, device):
     torch.manual_seed(args.seed)
-    teacher = tiny_mlp_sr().to(device)
     model = tiny_mlp_sr().to(device)
     opt = torch.optim.SGD(model.parameters(), lr=args.lr, momentum=0.9)
     group = None
     if mode != "nocompress":
         group = LowBitGroup(bitwidth=args.bitwidth, stochastic_rounding=(mode == "sr"))
-    g = torch.Generator(device=device).manual_seed(args.seed + 7919 * rank)
+    data = local_dataset(args, rank)
     losses = []
-    for _ in range(args.steps):
-        x = torch.randn(args.batch, 256, device=device, generator=g)
-        with torch.no_grad():
-            y = teacher(x).argmax(dim=1)
+    for step in range(args.steps):
+        x, y = batch_at(step, args, data, device)
         loss = nn.functional.cross_entropy(model(x), y)
         opt.zero_grad(set_to_none=True)
         loss.backward()
@@ -54,7 +71,8 @@ def run(mode, args, rank, world, device):
             else:
                 group.all_reduce(p.grad)
             p.grad.div_(world)
-        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        if args.grad_clip_norm > 0:
+            torch.nn.utils.clip_grad_norm_(model.parameters(), args.grad_clip_norm)
         opt.step()
         lt = loss.detach().clone()
         dist.all_reduce(lt)
@@ -69,6 +87,9 @@ def main():
     p.add_argument("--batch", type=int, default=128)
     p.add_argument("--lr", type=float, default=0.05)
     p.add_argument("--seed", type=int, default=2026)
+    p.add_argument("--data-seed", type=int, default=7)
+    p.add_argument("--dataset-size", type=int, default=8192)
+    p.add_argument("--grad-clip-norm", type=float, default=1.0)
     p.add_argument("--out", default=None)
     args = p.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -23,6 +23,20 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "performance: timing-sensitive test (BITSCOM_RUN_PERF=1)")
 
 
+GPU_TEST_TIMEOUT_S = 600  # wall-clock limit of one GPU test (pytest-timeout)
+
+
+def pytest_collection_modifyitems(config, items):
+    """Give every GPU test a hard wall-clock limit when pytest-timeout is
+    installed (the kernels' own waits are bounded; this also bounds host-side
+    hangs such as a missing peer process)."""
+    if not config.pluginmanager.hasplugin("timeout"):
+        return
+    for item in items:
+        if item.get_closest_marker("gpu") is not None and item.get_closest_marker("timeout") is None:
+            item.add_marker(pytest.mark.timeout(GPU_TEST_TIMEOUT_S))
+
+
 @pytest.fixture
 def run_perf_enabled():
     return os.getenv("BITSCOM_RUN_PERF", "0") == "1"

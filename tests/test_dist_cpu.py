@@ -280,3 +280,46 @@ def test_missing_rank_is_detected_by_timeout():
     res = run_ranks(_w_failure, 2, timeout=60)
     assert res[1] == "skipped"
     assert res[0].startswith("raised")
+
+
+def _w_fsdp2(rank, world, backend):
+    import torch.nn as nn
+    from torch.distributed.device_mesh import DeviceMesh
+    from torch.distributed.fsdp import fully_shard
+
+    if backend == "lowbit":
+        import bitscom_b200 as bitscom
+
+        bitscom.init(bitwidth=4, error_feedback=False)
+    dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    mesh = DeviceMesh.from_group(dist.group.WORLD, "cpu")
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(64, 128), nn.ReLU(), nn.Linear(128, 10))
+    fully_shard(model, mesh=mesh)
+    opt = torch.optim.SGD(model.parameters(), lr=0.1)
+    g = torch.Generator().manual_seed(rank)
+    losses = []
+    for _ in range(4):
+        x, y = torch.randn(32, 64, generator=g), torch.randint(0, 10, (32,), generator=g)
+        loss = nn.functional.cross_entropy(model(x), y)
+        loss.backward()
+        opt.step()
+        opt.zero_grad()
+        losses.append(float(loss.detach()))
+    stats = {}
+    if backend == "lowbit":
+        stats = dict(dist.group.WORLD._get_backend(torch.device("cpu")).stats())
+    dist.destroy_process_group()
+    return losses, stats
+
+
+def test_fsdp2_runs_over_lowbit_backend():
+    """FSDP2 (fully_shard) on a `lowbit` process group: its reduce-scatter and
+    all-gather reach the backend's tensor overrides, which forward CPU tensors
+    to the inner gloo group (the fused low-bit kernels take CUDA tensors), so
+    training matches plain gloo exactly."""
+    ref = run_ranks(_w_fsdp2, 2, ("gloo",))
+    got = run_ranks(_w_fsdp2, 2, ("lowbit",))
+    for r in range(2):
+        assert got[r][0] == ref[r][0]
+    assert got[0][1]["forwarded_calls"] > 0

@@ -27,7 +27,7 @@ import torch.distributed as dist
 from .. import _ext
 
 ALGOS = {"auto": 0, "twoshot": 1, "oneshot": 2}
-FMTS = {"int": 0, "e4m3": 1}
+FMTS = {"int": 0, "e4m3": 1, "sign": 2}  # "sign": 1-bit sign codes with a mean-|x| block scale
 
 _CACHE: Dict[Tuple[str, int], Optional["Communicator"]] = {}
 _LOCK = threading.Lock()

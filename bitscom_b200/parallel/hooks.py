@@ -42,6 +42,9 @@ class LowBitHookState:
         seed: Philox key of stochastic rounding.
         residual_dtype: element type of the EF residuals (torch.float32 or
             torch.bfloat16; bf16 halves their HBM traffic inside the kernel).
+        sign_1bit: with bitwidth 1, send sign codes with a mean-|x| block
+            scale (error-feedback signSGD) instead of the reference's
+            unsigned {0, 1} codes, which drop every negative value.
     """
 
     def __init__(
@@ -57,6 +60,7 @@ class LowBitHookState:
         seed: int = 0x5EED,
         use_comm_stream: bool = True,
         residual_dtype: torch.dtype = torch.float32,
+        sign_1bit: bool = False,
     ):
         if bitwidth not in (1, 2, 4, 8, 12, 16):
             raise ValueError(f"bitwidth must be one of (1, 2, 4, 8, 12, 16), got {bitwidth}")
@@ -73,6 +77,9 @@ class LowBitHookState:
         if residual_dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("residual_dtype must be torch.float32 or torch.bfloat16")
         self.residual_dtype = residual_dtype
+        if sign_1bit and bitwidth != 1:
+            raise ValueError("sign_1bit needs bitwidth=1")
+        self.sign_1bit = sign_1bit
         self.calls = 0
         self.residuals: Dict[int, torch.Tensor] = {}
         self._comms: Dict[int, Optional[Communicator]] = {}
@@ -161,7 +168,7 @@ def lowbit_allreduce_hook(state: LowBitHookState, bucket: dist.GradBucket) -> to
         comm.all_reduce(
             buf,
             bits=state.bitwidth,
-            fmt="e4m3" if state.fp8 else "int",
+            fmt="e4m3" if state.fp8 else ("sign" if state.sign_1bit else "int"),
             residual=residual,
             stochastic_rounding=state.stochastic_rounding,
             stochastic_requant=state.stochastic_rounding,

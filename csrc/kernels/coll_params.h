@@ -30,6 +30,7 @@ enum CollOp : int {
 enum WireFmt : int {
   kFmtInt = 0,   // signed integer codes (1-bit: unsigned {0,1}), per-block absmax scale
   kFmtE4M3 = 1,  // fp8 E4M3 codes with a per-block fp32 scale (absmax / 448)
+  kFmtSign = 2,  // 1-bit sign codes (1: x >= 0 -> +scale, 0: -scale), scale = mean |x| of the block
 };
 
 // Status bits written to the host-mapped status word.

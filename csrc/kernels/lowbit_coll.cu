@@ -231,6 +231,22 @@ struct Codec<B, kFmtInt> {
   }
 };
 
+// Sign-magnitude 1 bit (error-feedback signSGD: Seide et al., Interspeech
+// 2014; Karimireddy et al., ICML 2019): code = (x >= 0), value = +-scale with
+// scale = mean |x| over the 1024-element block (see encode_block).  The
+// reference's 1-bit codes are unsigned {0, 1} and lose every negative value;
+// this format is the opt-in alternative for 1-bit gradients.
+template <int B>
+struct Codec<B, kFmtSign> {
+  static_assert(B == 1, "sign codes are 1 bit");
+  __device__ __forceinline__ static uint32_t encode(float x, bool, uint32_t, float scale, float& deq) {
+    const uint32_t c = (x >= 0.0f) ? 1u : 0u;
+    deq = c ? scale : -scale;
+    return c;
+  }
+  __device__ __forceinline__ static float decode(uint32_t code, float scale) { return code ? scale : -scale; }
+};
+
 template <int B>
 struct Codec<B, kFmtE4M3> {
   static_assert(B == 8, "E4M3 codes are 8 bits");
@@ -274,12 +290,26 @@ template <int B, int FMT, int KEEP>
 __device__ __forceinline__ float encode_block(float (&v)[32], bool sr, uint64_t grp0, uint32_t stream,
                                               uint64_t seed, uint64_t offset, uint32_t (&w)[B]) {
   using C = Codec<B, FMT>;
-  float amax = 0.0f;
+  float scale, inv;
+  if constexpr (FMT == kFmtSign) {
+    // mean |x| of the block: per-lane sums in element order, then an xor
+    // butterfly (every lane ends with the same total: each pairwise sum is
+    // commutative), times 2^-10 (exact).
+    float s = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-  amax = warp_max(amax);
-  const float scale = C::scale_of(amax);
-  const float inv = 1.0f / scale;
+    for (int j = 0; j < 32; ++j) s = __fadd_rn(s, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    scale = __fmul_rn(s, 1.0f / static_cast<float>(kBlockElems));
+    inv = 1.0f;  // the sign codec reads only the sign of x * inv
+  } else {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = warp_max(amax);
+    scale = C::scale_of(amax);
+    inv = 1.0f / scale;
+  }
 #pragma unroll
   for (int i = 0; i < B; ++i) w[i] = 0u;
   // Stochastic rounding draws 16 bits per element: one Philox call (128
@@ -572,6 +602,12 @@ void dispatch_bits_fmt(int bits, int fmt, F&& f) {
     f(std::integral_constant<int, 8>{}, std::integral_constant<int, kFmtE4M3>{});
     return;
   }
+  if (fmt == kFmtSign) {
+    if (bits != 1) throw std::runtime_error("bitscom: the sign wire format needs bitwidth 1");
+    f(std::integral_constant<int, 1>{}, std::integral_constant<int, kFmtSign>{});
+    return;
+  }
+  if (fmt != kFmtInt) throw std::runtime_error("bitscom: unknown wire format");
   switch (bits) {
     case 1: f(std::integral_constant<int, 1>{}, std::integral_constant<int, kFmtInt>{}); break;
     case 2: f(std::integral_constant<int, 2>{}, std::integral_constant<int, kFmtInt>{}); break;
@@ -617,6 +653,8 @@ void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t
 cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int grid, cudaStream_t s) {
   if (p.world < 1 || p.world > kMaxRanks || grid < 1) return cudaErrorInvalidValue;
   if (p.fmt == kFmtE4M3 && bits != 8) return cudaErrorInvalidValue;
+  if (p.fmt == kFmtSign && bits != 1) return cudaErrorInvalidValue;
+  if (p.fmt != kFmtInt && p.fmt != kFmtE4M3 && p.fmt != kFmtSign) return cudaErrorInvalidValue;
   if (bits != 1 && bits != 2 && bits != 4 && bits != 8 && bits != 12 && bits != 16) return cudaErrorInvalidValue;
   if (dt != kF32 && dt != kBF16 && dt != kF16) return cudaErrorInvalidValue;
   if (p.res_dtype != kF32 && p.res_dtype != kBF16) return cudaErrorInvalidValue;

@@ -352,3 +352,32 @@ def test_launch_timing_in_stats(cuda):
     c.all_reduce(t, bits=4)
     torch.cuda.synchronize()
     assert c.stats()["timed_launches"] == 3
+
+
+@pytest.mark.parametrize("algo", ["twoshot", "oneshot"])
+@pytest.mark.parametrize("n", [1000, 50001, 3 * 8192 + 5])
+def test_sign_1bit_allreduce_matches_model(comm, algo, n):
+    """Opt-in sign-magnitude 1-bit format (mean-|x| block scale) with error
+    feedback, bit-exact against the CPU model."""
+    x = _x(n, seed=90 + n)
+    r = torch.randn(n) * 1e-4
+    t, rg = x.cuda(), r.cuda()
+    comm.all_reduce(t, bits=1, fmt="sign", algo=algo, residual=rg, post_scale=0.5)
+    torch.cuda.synchronize()
+    comm.check()
+    model = emu.allreduce_two_shot if algo == "twoshot" else emu.allreduce_one_shot
+    exp, res = model([x], 1, residuals=[r], post_scale=0.5, fmt="sign")
+    assert torch.equal(t.cpu(), exp)
+    assert torch.equal(rg.cpu(), res[0])
+
+
+def test_sign_1bit_reduce_scatter_all_gather(comm):
+    n = 20001
+    x = _x(n, seed=11)
+    out = torch.empty(n, device="cuda")
+    comm.reduce_scatter(out, x.cuda(), bits=1, fmt="sign")
+    g = torch.empty(n, device="cuda")
+    comm.all_gather(g, x.cuda(), bits=1, fmt="sign")
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), emu.reduce_scatter([x], 1, fmt="sign")[0])
+    assert torch.equal(g.cpu(), emu.all_gather([x], 1, fmt="sign"))

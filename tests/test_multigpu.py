@@ -69,6 +69,7 @@ CASES = [
     (123457, 16, "twoshot", "int", False, "float32"),
     (100000, 8, "twoshot", "e4m3", False, "float32"),
     (100000, 4, "twoshot", "int", False, "bfloat16"),
+    (77777, 1, "twoshot", "sign", True, "float32"),
 ]
 
 

@@ -97,3 +97,26 @@ def test_tuning_table_thresholds(tmp_path, monkeypatch):
     tuning.load_table.cache_clear()
     assert tuning.oneshot_max_bytes(2) == tuning.FALLBACK_ONESHOT_MAX_BYTES
     tuning.load_table.cache_clear()
+
+
+def test_sign_block_model_scale_and_error():
+    """CPU model of the sign-magnitude 1-bit format: the block scale is the
+    mean |x| (summed in the kernel's order), and on N(0, 1) data one 1-bit
+    sign pass has relative L2 error sqrt(1 - 2/pi) ~ 0.60, far below the
+    reference's unsigned 1-bit codes, which zero every negative value."""
+    import math
+
+    import torch
+
+    from tests import wire_emulator as emu
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(64 * 1024, generator=g)
+    scale = emu._block_mean_abs(x.view(-1, 1024)).view(-1)
+    torch.testing.assert_close(scale, x.view(-1, 1024).abs().mean(dim=1), rtol=1e-5, atol=0)
+    d = emu.block_quant(x, 1, "sign")
+    assert torch.equal(d.abs().view(-1, 1024), scale.unsqueeze(1).expand(-1, 1024))
+    rel = float((d - x).norm() / x.norm())
+    assert abs(rel - math.sqrt(1 - 2 / math.pi)) < 0.01
+    rel_unsigned = float((emu.block_quant(x, 1, "int") - x).norm() / x.norm())
+    assert rel_unsigned > rel + 0.1

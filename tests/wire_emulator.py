@@ -23,9 +23,26 @@ def _bounds(bits):
     return -(1 << (bits - 1)), (1 << (bits - 1)) - 1
 
 
+def _block_mean_abs(xb: torch.Tensor) -> torch.Tensor:
+    """The kernel's mean |x| per block, in its exact fp32 order: lane l sums
+    its 32 elements (k*32+l)*4+m in (k, m) order, then an xor butterfly over
+    the lanes (offsets 16, 8, 4, 2, 1), then times 2^-10."""
+    a = xb.abs().view(-1, 8, 32, 4).permute(0, 2, 1, 3).reshape(-1, 32, 32)  # [block, lane, j]
+    s = torch.zeros(a.shape[0], 32, dtype=torch.float32)
+    for j in range(32):
+        s = s + a[:, :, j]
+    lanes = torch.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        s = s + s[:, lanes ^ o]
+    return (s[:, :1] * (1.0 / BLOCK)).to(torch.float32)
+
+
 def block_quant(x: torch.Tensor, bits: int, fmt: str = "int") -> torch.Tensor:
     """Dequantised values of x (float32, length a multiple of BLOCK)."""
     xb = x.view(-1, BLOCK)
+    if fmt == "sign":
+        scale = _block_mean_abs(xb)
+        return torch.where(xb >= 0, scale, -scale).view(-1)
     amax = xb.abs().amax(dim=1, keepdim=True)
     one = torch.ones((), dtype=torch.float32)
     if fmt == "e4m3":

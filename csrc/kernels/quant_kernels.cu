@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kThreads)
 // quantise (+ pack) in the reference layout
 // ---------------------------------------------------------------------------
 template <typename T, int B, bool SR>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
     quantize_ref_kernel(const T* __restrict__ x, int64_t n, const uint32_t* __restrict__ amax_bits,
                         uint64_t seed, uint64_t offset, uint8_t* __restrict__ packed,
                         int16_t* __restrict__ q16, double* __restrict__ scale_out, bool vec_in,
@@ -521,7 +521,9 @@ void quantize_ref(const void* x, DType dt, int64_t n, int bits, const uint32_t* 
                   double* scale_out, cudaStream_t s) {
   if (n <= 0) return;
   const int64_t plen = packed_bytes_ref(n, bits);
-  const int g = grid_for((n + kTile - 1) / kTile, kWarps, 4);
+  // Three CTAs per SM (the kernel is bounded to 85 registers): the grid is
+  // exactly one resident wave.
+  const int g = grid_for((n + kTile - 1) / kTile, kWarps, 3);
   dispatch_dtype(dt, [&](auto tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
     dispatch_bits(bits, [&](auto bc) {

@@ -120,3 +120,21 @@ def test_sign_block_model_scale_and_error():
     assert abs(rel - math.sqrt(1 - 2 / math.pi)) < 0.01
     rel_unsigned = float((emu.block_quant(x, 1, "int") - x).norm() / x.norm())
     assert rel_unsigned > rel + 0.1
+
+
+def test_clock_sampler_summary_from_rows():
+    """The clock summary attached to bench lines: median SM clock over samples
+    under load, the max clock, and every throttle reason seen active."""
+    from bitscom_b200.utils.clocks import ClockSampler
+
+    cs = ClockSampler([0])
+    cs.rows = [
+        ["0", "1965", "1965", "300", "5", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"],
+        ["0", "1800", "1965", "990", "100", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+        ["0", "1700", "1965", "995", "99", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+        ["0", "1750", "1965", "998", "97", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"],
+    ]
+    s = cs.summary()
+    assert s["sm_mhz"] == 1750 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"]
+    assert ClockSampler([0]).summary()["reasons"] == ["unsampled"]

@@ -5,8 +5,9 @@ Counterpart of reference benchmarks/multimodel_stochastic_e2e_curve.py
 (published: multimodel_*_loss_curve_bw4.csv, multimodel_throughput_summary_bw4.csv).
 Differences by design: gradients go through the DDP comm hook (one fused
 kernel per bucket, overlapped with backward) instead of a hand-built bucket
-loop after backward (`--sync bucketed` restores that loop, driving
-LowBitGroup.all_reduce); the no-compression mode is a real fp32 all-reduce;
+loop after backward (`--sync bucketed` restores that loop with persistent
+buckets, GradBucketer over LowBitGroup.all_reduce); the no-compression mode
+is a real fp32 all-reduce;
 timing is device-side (CUDA events, max over ranks).
 
 BASELINE config 4 (ResNet-50 ImageNet shape, 2-bit EF + SR, 25 MB buckets,
@@ -90,14 +91,17 @@ def run(name, mode, args, rank, world, device):
     model = build(name, args).to(device)
     ddp = nn.parallel.DistributedDataParallel(model, device_ids=[device.index], bucket_cap_mb=args.bucket_mb,
                                               gradient_as_bucket_view=True)
-    group = None
+    bucketer = None
     if mode != "no_compression":
         sr = mode == "lowbit_sr"
         if args.sync == "ddp_hook":
             bitscom.register_lowbit_hook(ddp, bitwidth=args.bitwidth, error_feedback=not args.no_ef,
                                          stochastic_rounding=sr)
         else:
+            from bitscom_b200.parallel.bucketing import GradBucketer
+
             group = bitscom.LowBitGroup(bitwidth=args.bitwidth, stochastic_rounding=sr, error_feedback=not args.no_ef)
+            bucketer = GradBucketer(model.parameters(), group, bucket_mb=args.bucket_mb)
     opt = torch.optim.AdamW(model.parameters(), lr=args.lr, weight_decay=0.01, fused=True)
     warm = max(1, int(args.steps * 0.1))
     sched = torch.optim.lr_scheduler.LambdaLR(
@@ -118,19 +122,10 @@ def run(name, mode, args, rank, world, device):
             a.record()
         batch = data[step % len(data)]
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = loss_of(name, ddp if group is None else model, batch)
-        if group is None:
-            loss.backward()
-        else:  # reference-style: backward without DDP, then bucketed low-bit all-reduce
-            loss.backward()
-            grads = [p.grad for p in model.parameters() if p.grad is not None]
-            flat = torch.cat([g.reshape(-1) for g in grads])
-            group.all_reduce(flat, ef_key=name)
-            flat.div_(world)
-            off = 0
-            for g in grads:
-                g.copy_(flat[off : off + g.numel()].view_as(g))
-                off += g.numel()
+            loss = loss_of(name, ddp if bucketer is None else model, batch)
+        loss.backward()
+        if bucketer is not None:  # reference-style: backward without DDP, then bucketed low-bit all-reduce
+            bucketer.sync()
         torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
         opt.step()
         sched.step()

@@ -323,3 +323,44 @@ def test_fsdp2_runs_over_lowbit_backend():
     for r in range(2):
         assert got[r][0] == ref[r][0]
     assert got[0][1]["forwarded_calls"] > 0
+
+
+def _w_bucketer(rank, world, bits):
+    import torch.nn as nn
+
+    from bitscom_b200 import LowBitGroup
+    from bitscom_b200.parallel.bucketing import GradBucketer
+
+    _init_gloo(rank, world)
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(32, 64), nn.ReLU(), nn.Linear(64, 64), nn.ReLU(), nn.Linear(64, 5))
+    bk = GradBucketer(model.parameters(), LowBitGroup(bitwidth=bits, error_feedback=True), bucket_mb=0.01)
+    g = torch.Generator().manual_seed(100 + rank)
+    x, y = torch.randn(16, 32, generator=g), torch.randint(0, 5, (16,), generator=g)
+    nn.functional.cross_entropy(model(x), y).backward()
+    views_ok = all(
+        any(buf.data_ptr() <= p.grad.data_ptr() < buf.data_ptr() + buf.numel() * buf.element_size() for buf in bk.buffers)
+        for p in model.parameters()
+    )
+    local = [p.grad.clone() for p in model.parameters()]
+    bk.sync()
+    synced = [p.grad.clone() for p in model.parameters()]
+    bk.zero_grad()
+    zeroed = all(float(p.grad.abs().sum()) == 0.0 for p in model.parameters())
+    dist.destroy_process_group()
+    return bk.num_buckets(), views_ok, local, synced, zeroed
+
+
+@pytest.mark.parametrize("bits", [16, 4])
+def test_grad_bucketer(bits):
+    res = run_ranks(_w_bucketer, 2, (bits,))
+    nb, views_ok, _, _, zeroed = res[0]
+    assert nb > 1 and views_ok and zeroed
+    for i in range(len(res[0][2])):
+        mean = (res[0][2][i] + res[1][2][i]) / 2
+        a, b = res[0][3][i], res[1][3][i]
+        assert torch.equal(a, b)  # every rank holds the same reduced gradient
+        if bits == 16:  # >= 8 bits: full-precision all-reduce
+            torch.testing.assert_close(a, mean, rtol=1e-6, atol=1e-7)
+        else:
+            assert float((a - mean).norm()) <= 0.5 * float(mean.norm()) + 1e-6

@@ -15,12 +15,12 @@ with a persistent error-feedback residual per bucket) and averages.
 
 from __future__ import annotations
 
-from typing import Iterable, List, Optional
+from typing import TYPE_CHECKING, Iterable, List, Optional
 
 import torch
-import torch.distributed as dist
 
-from ..api import LowBitGroup
+if TYPE_CHECKING:  # the api module imports this package
+    from ..api import LowBitGroup
 
 
 class GradBucketer:
@@ -40,9 +40,13 @@ class GradBucketer:
     :meth:`zero_grad` here).
     """
 
-    def __init__(self, params: Iterable[torch.nn.Parameter], group: Optional[LowBitGroup] = None,
+    def __init__(self, params: Iterable[torch.nn.Parameter], group: Optional["LowBitGroup"] = None,
                  bucket_mb: float = 25.0, average: bool = True):
-        self.group = group if group is not None else LowBitGroup(bitwidth=4, error_feedback=True)
+        if group is None:
+            from ..api import LowBitGroup
+
+            group = LowBitGroup(bitwidth=4, error_feedback=True)
+        self.group = group
         self.average = average
         ps = [p for p in params if p.requires_grad]
         if not ps:

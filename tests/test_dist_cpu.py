@@ -364,3 +364,34 @@ def test_grad_bucketer(bits):
             torch.testing.assert_close(a, mean, rtol=1e-6, atol=1e-7)
         else:
             assert float((a - mean).norm()) <= 0.5 * float(mean.norm()) + 1e-6
+
+
+def _w_backend_views(rank, world):
+    import bitscom_b200 as bitscom
+
+    bitscom.init(bitwidth=4, error_feedback=False)
+    dist.init_process_group("lowbit", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    g = torch.Generator().manual_seed(40 + rank)
+    base = torch.randn(64, 65, generator=g)
+    base_in = base.clone()
+    t = base.t()  # non-contiguous view
+    assert not t.is_contiguous()
+    dist.all_reduce(t)
+    b16 = (torch.randn(3001, generator=g) * 0.1).to(torch.bfloat16)
+    b16_in = b16.clone()
+    dist.all_reduce(b16)
+    dist.destroy_process_group()
+    return base_in, t.clone(), b16_in, b16
+
+
+def test_native_backend_staged_path_views_and_bf16():
+    """The staged (CPU) path on a non-contiguous view and on bf16 tensors:
+    values reduced in logical element order, results written back in place
+    and rounded to the tensor's dtype."""
+    res = run_ranks(_w_backend_views, 2)
+    exp, _ = c15_oracle([r[0].t().reshape(-1) for r in res], 4)
+    exp16, _ = c15_oracle([r[2].float() for r in res], 4)
+    for r in range(2):
+        assert (res[r][1].reshape(-1) - exp).abs().max() < 1e-5
+        assert res[r][3].dtype == torch.bfloat16
+        assert torch.equal(res[r][3], exp16.to(torch.bfloat16))

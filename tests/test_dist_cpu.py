@@ -395,3 +395,35 @@ def test_native_backend_staged_path_views_and_bf16():
         assert (res[r][1].reshape(-1) - exp).abs().max() < 1e-5
         assert res[r][3].dtype == torch.bfloat16
         assert torch.equal(res[r][3], exp16.to(torch.bfloat16))
+
+
+def _w_rs_ag_tensor(rank, world):
+    from bitscom_b200 import LowBitGroup
+
+    _init_gloo(rank, world)
+    grp = LowBitGroup(bitwidth=4)
+    g = torch.Generator().manual_seed(70 + rank)
+    x = torch.randn(2 * 1000, generator=g)
+    rs = torch.empty(1000)
+    grp.reduce_scatter_tensor(rs, x)
+    rs_avg = torch.empty(1000)
+    grp.reduce_scatter_tensor(rs_avg, x, average=True)
+    ag = torch.empty(2 * 2000)
+    grp.all_gather_into_tensor(ag, x)
+    dist.destroy_process_group()
+    return x, rs, rs_avg, ag
+
+
+def test_lowbitgroup_tensor_rs_ag_on_cpu():
+    """Without the fused kernel (CPU tensors) the tensor reduce-scatter and
+    all-gather quantise each rank's input with the reference's per-tensor
+    4-bit roundtrip and then reduce / gather in full precision."""
+    from bitscom_b200.quantization import roundtrip_tensor
+
+    res = run_ranks(_w_rs_ag_tensor, 2)
+    q = [roundtrip_tensor(r[0], 4) for r in res]
+    total = q[0] + q[1]
+    for r in range(2):
+        torch.testing.assert_close(res[r][1], total[r * 1000 : (r + 1) * 1000], rtol=1e-6, atol=1e-6)
+        torch.testing.assert_close(res[r][2], total[r * 1000 : (r + 1) * 1000] / 2, rtol=1e-6, atol=1e-6)
+        assert torch.equal(res[r][3], torch.cat(q))

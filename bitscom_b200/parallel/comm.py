@@ -16,6 +16,7 @@ every rank (like NCCL).
 
 from __future__ import annotations
 
+import contextlib
 import os
 import socket
 import threading
@@ -28,6 +29,14 @@ from .. import _ext
 
 ALGOS = {"auto": 0, "twoshot": 1, "oneshot": 2}
 FMTS = {"int": 0, "e4m3": 1, "sign": 2}  # "sign": 1-bit sign codes with a mean-|x| block scale
+
+def _trace_range(name: str):
+    """A ``lowbit:<name>`` profiler range while torch.profiler records (the
+    trace analyzer attributes these to communication), nothing otherwise."""
+    if torch.autograd.profiler._is_profiler_enabled:
+        return torch.autograd.profiler.record_function("lowbit:" + name)
+    return contextlib.nullcontext()
+
 
 _CACHE: Dict[Tuple[str, int], Optional["Communicator"]] = {}
 _LOCK = threading.Lock()
@@ -199,10 +208,11 @@ class Communicator:
         feedback: the kernel quantises ``tensor + residual`` and writes the new
         residual.
         """
-        self._c.allreduce(
-            tensor, out, residual, bits, FMTS[fmt], ALGOS[algo], stochastic_rounding, stochastic_requant,
-            int(seed), int(offset), float(post_scale), int(max_ctas),
-        )
+        with _trace_range("all_reduce"):
+            self._c.allreduce(
+                tensor, out, residual, bits, FMTS[fmt], ALGOS[algo], stochastic_rounding, stochastic_requant,
+                int(seed), int(offset), float(post_scale), int(max_ctas),
+            )
         return tensor if out is None else out
 
     def reduce_scatter(
@@ -220,10 +230,11 @@ class Communicator:
         max_ctas: int = 0,
     ) -> torch.Tensor:
         """Low-bit SUM reduce-scatter: ``input`` holds world*n elements, ``output`` n."""
-        self._c.reduce_scatter(
-            input, output, residual, bits, FMTS[fmt], stochastic_rounding, int(seed), int(offset),
-            float(post_scale), int(max_ctas),
-        )
+        with _trace_range("reduce_scatter"):
+            self._c.reduce_scatter(
+                input, output, residual, bits, FMTS[fmt], stochastic_rounding, int(seed), int(offset),
+                float(post_scale), int(max_ctas),
+            )
         return output
 
     def all_gather(
@@ -240,7 +251,8 @@ class Communicator:
         max_ctas: int = 0,
     ) -> torch.Tensor:
         """Low-bit all-gather: ``output`` holds world*n elements (rank-major)."""
-        self._c.all_gather(
-            input, output, residual, bits, FMTS[fmt], stochastic_rounding, int(seed), int(offset), int(max_ctas)
-        )
+        with _trace_range("all_gather"):
+            self._c.all_gather(
+                input, output, residual, bits, FMTS[fmt], stochastic_rounding, int(seed), int(offset), int(max_ctas)
+            )
         return output

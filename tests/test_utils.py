@@ -138,3 +138,19 @@ def test_clock_sampler_summary_from_rows():
     assert s["sm_mhz"] == 1750 and s["sm_max_mhz"] == 1965
     assert s["reasons"] == ["sw_power_cap"]
     assert ClockSampler([0]).summary()["reasons"] == ["unsampled"]
+
+
+def test_trace_ranges_only_while_profiling():
+    import contextlib
+
+    import torch
+
+    from bitscom_b200.parallel.comm import _trace_range
+    from bitscom_b200.utils.trace import is_comm
+
+    assert isinstance(_trace_range("all_reduce"), contextlib.nullcontext)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU]) as prof:
+        with _trace_range("all_reduce"):
+            torch.ones(3).add_(1)
+    names = [e.name for e in prof.events()]
+    assert "lowbit:all_reduce" in names and is_comm("lowbit:all_reduce")

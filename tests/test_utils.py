@@ -154,3 +154,10 @@ def test_trace_ranges_only_while_profiling():
             torch.ones(3).add_(1)
     names = [e.name for e in prof.events()]
     assert "lowbit:all_reduce" in names and is_comm("lowbit:all_reduce")
+
+
+def test_info_entry_point_runs():
+    from bitscom_b200.__main__ import info
+
+    d = info()
+    assert d["bitscom_b200"] and "tuning" in d and isinstance(d["devices"], list)

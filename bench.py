@@ -165,6 +165,8 @@ def build_ours(args, rank, world, local):
                 n += c.stats()["launches"]
         return n
 
+    _MODEL[0] = model
+    _COMMS[0] = state._comms
     return step, launches, "bitscom_b200 DDP comm hook (fused sm_100a NVLink kernel)"
 
 
@@ -204,7 +206,9 @@ def build_reference(args, rank, world, local):
     model = model.cuda().to(memory_format=torch.channels_last)
     for p in model.parameters():  # same initial weights on every rank
         dist.broadcast(p.data, 0)
-    opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9)
+    # Same torch optimizer settings as our arm (fused SGD is a torch choice,
+    # not library work).
+    opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True)
     cap = int(args.bucket_mb * 2**20 / 4)
     params = [p for p in model.parameters()]
     buckets, cur, size = [], [], 0
@@ -246,9 +250,46 @@ def build_reference(args, rank, world, local):
         opt.zero_grad(set_to_none=False)
         return loss
 
+    _MODEL[0] = model
     desc = ("reference bitscom lowbit backend, error feedback, dist.all_reduce per persistent bucket after backward"
             if group is None else "reference bitscom LowBitGroup over NCCL, bucketed after backward (no EF)")
     return step, (lambda: 0), desc
+
+
+_MODEL = [None]  # the trained module of the arm (for the replica check)
+_COMMS = [None]  # our arm: the hook's communicators (for kernel timing)
+
+
+def replicas_identical(world: int):
+    """After the run: do all ranks hold bit-identical parameters?  (float64
+    sum and sum of squares of every parameter, gathered over ranks.)"""
+    if world == 1 or _MODEL[0] is None:
+        return None
+    with torch.no_grad():
+        v = torch.stack([torch.stack([p.double().sum(), p.double().square().sum()]) for p in _MODEL[0].parameters()])
+    allv = [torch.empty_like(v) for _ in range(world)]
+    dist.all_gather(allv, v, group=aux_group())
+    return bool(all(torch.equal(allv[0], a) for a in allv[1:]))
+
+
+def fused_kernel_ms(step, xs_dev, ys_dev, n, world):
+    """Device time of the fused collective launches per eager step (CUDA
+    events around every launch), over n untimed steps; max over ranks."""
+    comms = [c for c in (_COMMS[0] or {}).values() if c is not None]
+    if not comms:
+        return None
+    for c in comms:
+        c.native.reset_stats()
+        c.set_timing(True)
+    for i in range(n):
+        step(xs_dev[i % POOL], ys_dev[i % POOL])
+    torch.cuda.synchronize()
+    ms = 0.0
+    for c in comms:
+        st = c.stats()
+        ms += st["kernel_ms"]
+        c.set_timing(False)
+    return max_over_ranks(ms / n, world)
 
 
 # ----------------------------------------------------------------------------
@@ -300,6 +341,7 @@ def main():
 
     graph = args.impl == "ours" and not args.eager and args.hook == "lowbit"
     bufs = None
+    kernel_ms = None
     per_step_launches = None
     if graph:
         # Whole-step CUDA graph (forward, backward with the fused all-reduce
@@ -312,6 +354,9 @@ def main():
         with torch.cuda.stream(side):
             for i in range(DDP_EAGER_WARMUP):
                 step(xs_dev[i % POOL], ys_dev[i % POOL])
+            # Fused-kernel device time per step, from eager warm-up steps
+            # (launches inside a replayed graph are not timed).
+            kernel_ms = fused_kernel_ms(step, xs_dev, ys_dev, 5, world)
         torch.cuda.current_stream().wait_stream(side)
         barrier_sync(world)
         la = launches()
@@ -355,6 +400,9 @@ def main():
             "h2d_bytes_per_step": int(img_bytes),
             "d2h_bytes_per_step": 4,
         }
+    if args.impl == "ours" and not graph and args.hook == "lowbit":
+        kernel_ms = fused_kernel_ms(step, xs_dev, ys_dev, 5, world)
+    identical = replicas_identical(world)
     value = args.batch * world * args.steps / (ms / 1e3)
     clocks = cs.summary()
     if rank == 0:
@@ -391,6 +439,11 @@ def main():
             "clocks": {"sm_mhz": clocks.get("sm_mhz"), "sm_max_mhz": clocks.get("sm_max_mhz"), "reasons": clocks.get("reasons")},
             "gpu_launches": int(l1 - l0),
         }
+        if kernel_ms is not None:
+            out["fused_kernel_ms_per_step"] = round(kernel_ms, 4)
+            out["fused_kernel_ms_note"] = "device time of the fused all-reduce launches of one eager step (CUDA events), max over ranks"
+        if identical is not None:
+            out["replicas_identical"] = identical
         if args.impl == "reference":
             out["impl"] = "reference"
         if e2e is not None:

@@ -108,7 +108,13 @@ class LowBitGroup:
         self.use_fused = use_fused
         self.seed = int(seed)
         self._calls = 0
+        # Error-feedback residuals by key: the caller's ``ef_key``, or
+        # ("auto", i) for the i-th distinct tensor (storage, offset, size)
+        # all-reduced without a key, so a resumed run that issues its calls in
+        # the same order finds its residuals again.
         self._residuals: Dict[object, torch.Tensor] = {}
+        self._auto_keys: Dict[tuple, int] = {}
+        self._pending: Dict[object, torch.Tensor] = {}  # restored, not used yet
 
     # ------------------------------------------------------------------ info
     @property
@@ -131,8 +137,16 @@ class LowBitGroup:
     def _residual(self, t: torch.Tensor, key=None) -> Optional[torch.Tensor]:
         if not self.error_feedback:
             return None
-        k = key if key is not None else (t.untyped_storage().data_ptr(), t.storage_offset(), t.numel(), t.device)
+        k = key
+        if k is None:
+            ident = (t.untyped_storage().data_ptr(), t.storage_offset(), t.numel(), str(t.device))
+            idx = self._auto_keys.setdefault(ident, len(self._auto_keys))
+            k = ("auto", idx)
         r = self._residuals.get(k)
+        if r is None and k in self._pending:
+            r = self._pending.pop(k)
+            if r.numel() == t.numel():
+                r = self._residuals[k] = r.to(device=t.device, dtype=torch.float32).contiguous()
         if r is None or r.numel() != t.numel() or r.device != t.device:
             r = torch.zeros(t.numel(), dtype=torch.float32, device=t.device)
             self._residuals[k] = r
@@ -257,7 +271,13 @@ class LowBitGroup:
             x = torch.cat([x, x.new_zeros(pad)])
         shard = x.numel() // world
         sr = self.stochastic_rounding
-        q, scale = quantize_codes(x, bits, stochastic=sr, offset=self._next_offset())
+        # Philox keys of the two roundings: the group's seed, this rank and
+        # the phase, so stochastic rounding is reproducible (and resumable)
+        # and independent across ranks.
+        rank = dist.get_rank(group) if world > 1 else 0
+        seed1 = (self.seed ^ (rank << 40) ^ (1 << 56)) & (2**63 - 1)
+        seed2 = (self.seed ^ (rank << 40) ^ (2 << 56)) & (2**63 - 1)
+        q, scale = quantize_codes(x, bits, stochastic=sr, seed=seed1, offset=self._next_offset())
         if residual is not None:
             residual.copy_((x - q.to(torch.float32) * scale)[:n])
         send = torch.cat([pack_codes(q[s * shard : (s + 1) * shard], bits) for s in range(world)])
@@ -269,7 +289,7 @@ class LowBitGroup:
         local = torch.zeros(shard, dtype=torch.float32, device=x.device)
         for s in range(world):
             local.add_(unpack_dequant(recv[s * per : (s + 1) * per], bits, shard, scales_in[s : s + 1]))
-        packed_r, scale_r = quantize_pack(local, bits, stochastic=sr, offset=self._next_offset())
+        packed_r, scale_r = quantize_pack(local, bits, stochastic=sr, seed=seed2, offset=self._next_offset())
         gathered = torch.empty(world * packed_r.numel(), dtype=torch.uint8, device=x.device)
         dist.all_gather_into_tensor(gathered, packed_r, group=group)
         scales_r = torch.empty(world, dtype=torch.float32, device=x.device)
@@ -382,11 +402,23 @@ class LowBitGroup:
 
     # --------------------------------------------------------- EF state
     def state_dict(self) -> dict:
-        """Error-feedback residuals and the SR call counter (for checkpoints)."""
-        return {"calls": self._calls, "residuals": {str(k): v.detach().cpu() for k, v in self._residuals.items()}}
+        """Error-feedback residuals and the stochastic-rounding call counter.
+
+        Residuals are saved under their ``ef_key``, or under ("auto", i) for
+        the i-th distinct tensor all-reduced without one."""
+        res = dict(self._pending)
+        res.update(self._residuals)
+        return {"calls": self._calls, "residuals": {k: v.detach().cpu().clone() for k, v in res.items()}}
 
     def load_state_dict(self, state: dict) -> None:
+        """Restore a :meth:`state_dict`: each residual is attached to its key's
+        tensor on that tensor's first all-reduce (same ``ef_key``, or the same
+        position in the order of first use), so resumed training continues
+        bit-identically."""
         self._calls = int(state.get("calls", 0))
+        self._residuals = {}
+        self._auto_keys = {}
+        self._pending = {k: v.detach().clone() for k, v in state.get("residuals", {}).items()}
 
 
 __all__ = ["LowBitGroup", "packed_nbytes"]

@@ -12,11 +12,15 @@ communication stream (ordered after the gradient producers), so the low-bit
 all-reduce of bucket k overlaps the backward kernels of buckets k+1..; the
 returned CUDA-aware future completes in stream order.  Gradients are averaged
 inside the kernel (``post_scale = 1/world``), the error-feedback residual of
-each bucket lives in :class:`LowBitHookState` (keyed by bucket index, shape
-checked) and is checkpointable through ``state_dict()``.
+each bucket lives in :class:`LowBitHookState` and is checkpointable through
+``state_dict()``.  A residual is keyed by the bucket's index AND its parameter
+signature (the model-order indices of the bucket's parameters), so when DDP
+rebuilds its buckets after the first iteration a bucket with a new parameter
+set or order starts from a fresh residual instead of inheriting another
+bucket's errors element by element.
 """
 
-from typing import Dict, Optional
+from typing import Dict, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -81,7 +85,9 @@ class LowBitHookState:
             raise ValueError("sign_1bit needs bitwidth=1")
         self.sign_1bit = sign_1bit
         self.calls = 0
-        self.residuals: Dict[int, torch.Tensor] = {}
+        # (bucket index, parameter signature) -> residual
+        self.residuals: Dict[Tuple[int, Tuple], torch.Tensor] = {}
+        self._param_index: Dict[int, int] = {}
         self._comms: Dict[int, Optional[Communicator]] = {}
         self._streams: Dict[int, torch.cuda.Stream] = {}
 
@@ -105,15 +111,34 @@ class LowBitHookState:
             self._streams[idx] = torch.cuda.Stream(device=device, priority=-1)
         return self._streams[idx]
 
-    def residual(self, bucket_index: int, buf: torch.Tensor) -> Optional[torch.Tensor]:
+    def set_parameter_order(self, params) -> None:
+        """Index the model's parameters (``model.parameters()`` order); bucket
+        signatures then name parameters by these indices, which are the same
+        in every process that builds the same model (checkpoint resume)."""
+        self._param_index = {id(p): i for i, p in enumerate(params)}
+
+    def bucket_signature(self, bucket) -> Tuple:
+        """Model-order indices of the bucket's parameters, in bucket order
+        (their shapes when the parameter order is unknown)."""
+        params = bucket.parameters()
+        if self._param_index and all(id(p) in self._param_index for p in params):
+            return tuple(self._param_index[id(p)] for p in params)
+        return tuple(tuple(p.shape) for p in params)
+
+    def residual(self, bucket_index: int, buf: torch.Tensor, signature: Tuple = ()) -> Optional[torch.Tensor]:
         if not self.error_feedback:
             return None
-        r = self.residuals.get(bucket_index)
+        key = (int(bucket_index), tuple(signature))
+        r = self.residuals.get(key)
         if r is not None and r.numel() == buf.numel() and (r.device != buf.device or r.dtype != self.residual_dtype):
-            r = self.residuals[bucket_index] = r.to(buf.device, self.residual_dtype).contiguous()
+            r = self.residuals[key] = r.to(buf.device, self.residual_dtype).contiguous()
         if r is None or r.numel() != buf.numel():
+            # A bucket index with a new parameter signature: DDP rebuilt its
+            # buckets, so the residuals of the old layout of this index are stale.
+            for old in [k for k in self.residuals if k[0] == key[0]]:
+                del self.residuals[old]
             r = torch.zeros(buf.numel(), dtype=self.residual_dtype, device=buf.device)
-            self.residuals[bucket_index] = r
+            self.residuals[key] = r
         return r
 
     # ---------------------------------------------------------- checkpoint
@@ -128,7 +153,12 @@ class LowBitHookState:
         if int(state.get("bitwidth", self.bitwidth)) != self.bitwidth:
             raise ValueError("checkpoint was written with a different bitwidth")
         self.calls = int(state.get("calls", 0))
-        self.residuals = {int(k): v.clone() for k, v in state.get("residuals", {}).items()}
+        res = {}
+        for k, v in state.get("residuals", {}).items():
+            if not (isinstance(k, tuple) and len(k) == 2):
+                raise ValueError("checkpoint residual keys must be (bucket index, parameter signature) pairs")
+            res[(int(k[0]), tuple(k[1]))] = v.clone()
+        self.residuals = res
 
 
 def _staged_fallback(state: LowBitHookState, buf: torch.Tensor) -> torch.Tensor:
@@ -159,7 +189,7 @@ def lowbit_allreduce_hook(state: LowBitHookState, bucket: dist.GradBucket) -> to
         fut.set_result(_staged_fallback(state, buf))
         return fut
 
-    residual = state.residual(bucket.index(), buf)
+    residual = state.residual(bucket.index(), buf, state.bucket_signature(bucket) if state.error_feedback else ())
     cur = torch.cuda.current_stream(buf.device)
     stream = state.stream(buf.device) if state.use_comm_stream else cur
     if stream is not cur:
@@ -191,5 +221,6 @@ def register_lowbit_hook(ddp_model, **kwargs) -> LowBitHookState:
     """Create a :class:`LowBitHookState` and register the hook on a DDP model."""
     pg = kwargs.pop("process_group", None) or ddp_model.process_group
     state = LowBitHookState(process_group=pg, **kwargs)
+    state.set_parameter_order(ddp_model.module.parameters())
     ddp_model.register_comm_hook(state, lowbit_allreduce_hook)
     return state

@@ -26,12 +26,15 @@
 //   * the first call on a device performs a one-time set-up with that device
 //     current (it looks up the device address of the scratch array with
 //     cudaGetSymbolAddress and clears the scratch's counters and flags with
-//     cudaMemsetAsync on the given stream), so make the first call before any
-//     CUDA-graph capture on that device;
+//     cudaMemsetAsync on the given stream), so make the first call on a
+//     device before any stream capture begins on that device;
 //   * every call on a device shares the same scratch, which keeps the last
 //     call's contents: calls must be ordered on the GPU (one stream, or
 //     explicit dependencies).  Calls that overlap on the GPU race and produce
 //     wrong results.
+//   * a call returns as soon as its kernel is enqueued, so its return code
+//     covers argument checks, set-up and the launch only; a kernel that gave
+//     up waiting reports through bitscom_noalloc_status();
 //   * no cudaMalloc, cudaFree, host allocation or allocating library routine
 //     is called.
 #pragma once
@@ -57,6 +60,14 @@ long long bitscom_noalloc_max_elems(void);
 
 // Bytes of the static scratch array.
 long long bitscom_noalloc_scratch_bytes(void);
+
+// Status of the calls completed so far on the current device: 0 when every
+// kernel finished normally, otherwise the kernel's status bits (1 = a wait on
+// a completion flag gave up after its time limit; the output and residual of
+// that call are then incomplete).  A kernel writes the word only on failure,
+// so read it after synchronising with the calls it should cover; `reset` != 0
+// clears it.  Returns BITSCOM_NOALLOC_ECUDA if the read fails.  Synchronous.
+int bitscom_noalloc_status(int reset);
 
 // Human-readable message of an error code.
 const char* bitscom_noalloc_strerror(int code);

@@ -37,8 +37,12 @@ constexpr long long kScratchBytes = kDataOff + 4 * kRegionBytes;  // about 8.4 M
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
+constexpr int kStatusWord = 128;  // word index of the status word in the counter page
 std::mutex g_setup_mu;
-unsigned char* g_dev_ptr[kMaxDevices] = {};
+// Per-device scratch address, published with release ordering after the
+// other per-device fields, so a reader that sees a non-null pointer (acquire)
+// also sees the SM count and the epoch reset.
+std::atomic<unsigned char*> g_dev_ptr[kMaxDevices] = {};
 int g_sm_count[kMaxDevices] = {};
 std::atomic<uint32_t> g_epoch[kMaxDevices];
 
@@ -46,7 +50,7 @@ std::atomic<uint32_t> g_epoch[kMaxDevices];
 // SM count, and cleared counters/flags.  Returns false on a CUDA error.
 bool setup(int dev, cudaStream_t stream) {
   std::lock_guard<std::mutex> lk(g_setup_mu);
-  if (g_dev_ptr[dev] != nullptr) return true;
+  if (g_dev_ptr[dev].load(std::memory_order_acquire) != nullptr) return true;
   void* ptr = nullptr;
   if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return false;
   int sms = 0;
@@ -54,7 +58,7 @@ bool setup(int dev, cudaStream_t stream) {
   if (cudaMemsetAsync(ptr, 0, static_cast<size_t>(kDataOff), stream) != cudaSuccess) return false;
   g_sm_count[dev] = sms > 0 ? sms : 148;
   g_epoch[dev].store(0);
-  g_dev_ptr[dev] = static_cast<unsigned char*>(ptr);
+  g_dev_ptr[dev].store(static_cast<unsigned char*>(ptr), std::memory_order_release);
   return true;
 }
 
@@ -88,8 +92,11 @@ __attribute__((visibility("default"))) int bitscom_lowbit_allreduce_local_noallo
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BITSCOM_NOALLOC_ECUDA;
-  if (g_dev_ptr[dev] == nullptr && !setup(dev, stream)) return BITSCOM_NOALLOC_ECUDA;
-  unsigned char* base = g_dev_ptr[dev];
+  unsigned char* base = g_dev_ptr[dev].load(std::memory_order_acquire);
+  if (base == nullptr) {
+    if (!setup(dev, stream)) return BITSCOM_NOALLOC_ECUDA;
+    base = g_dev_ptr[dev].load(std::memory_order_acquire);
+  }
 
   CollParams p;
   std::memset(&p, 0, sizeof(p));
@@ -130,7 +137,7 @@ __attribute__((visibility("default"))) int bitscom_lowbit_allreduce_local_noallo
   p.done = counters + 32;
   p.abort_flag = counters + 64;
   p.fault_skip = counters + 96;
-  p.status = counters + 128;
+  p.status = counters + kStatusWord;
   p.timeout_ns = 10ull * 1000ull * 1000ull * 1000ull;  // world size 1 only waits on its own flags
 
   const long long items = 2 * n_sub;  // phase 1 + phase 2 at world size 1
@@ -138,6 +145,24 @@ __attribute__((visibility("default"))) int bitscom_lowbit_allreduce_local_noallo
   if (launch::lowbit_coll_nothrow(p, static_cast<DType>(dtype), bits, grid, stream) != cudaSuccess)
     return BITSCOM_NOALLOC_ECUDA;
   return BITSCOM_NOALLOC_OK;
+}
+
+__attribute__((visibility("default"))) int bitscom_noalloc_status(int reset) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BITSCOM_NOALLOC_ECUDA;
+  if (g_dev_ptr[dev].load(std::memory_order_acquire) == nullptr) return 0;  // no call yet on this device
+  // Synchronous copies from and to the scratch's status word (the status
+  // lives in device memory; these copies allocate nothing).
+  uint32_t v = 0;
+  const size_t off = static_cast<size_t>(kStatusWord) * sizeof(uint32_t);
+  if (cudaMemcpyFromSymbol(&v, g_noalloc_scratch, sizeof(v), off, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return BITSCOM_NOALLOC_ECUDA;
+  if (reset && v != 0u) {
+    const uint32_t zero = 0u;
+    if (cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(zero), off, cudaMemcpyHostToDevice) != cudaSuccess)
+      return BITSCOM_NOALLOC_ECUDA;
+  }
+  return static_cast<int>(v);
 }
 
 }  // extern "C"

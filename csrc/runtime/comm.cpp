@@ -96,6 +96,7 @@ LowBitComm::~LowBitComm() {
     cudaEventDestroy(pr.second);
   }
   for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+  if (order_ev_) cudaEventDestroy(order_ev_);
   for (int r = 0; r < world_; ++r)
     if (r != rank_ && opened_[r] && peers_[r]) cudaIpcCloseMemHandle(peers_[r]);
   if (ws_) cudaFree(ws_);
@@ -327,7 +328,14 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   // chunks still being encoded), so automatic means phase-major.
   p.lag = sched_lag_ >= 0 ? sched_lag_ : 0;
   DeviceGuard g(device_);
-  const bool timed = timing_ && !p.offset_from_epoch;  // never under capture
+  const bool capturing = p.offset_from_epoch != 0;
+  // Launches share the workspace, counters and epoch parity: one launch must
+  // finish before the next starts.  Launches on one stream are ordered by the
+  // stream; a launch on another stream (e.g. a DDP hook's comm stream and a
+  // LowBitGroup call on the caller's stream) first waits for the previous
+  // launch's completion event.  Captured launches are ordered by their graph.
+  if (!capturing && have_last_ && last_stream_ != s) ck(cudaStreamWaitEvent(s, order_ev_, 0), "cudaStreamWaitEvent");
+  const bool timed = timing_ && !capturing;  // never under capture
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   if (timed) {
     e0 = take_event();
@@ -339,6 +347,12 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
     ck(cudaEventRecord(e1, s), "cudaEventRecord");
     timed_.emplace_back(e0, e1);
     if (timed_.size() > 4096) collect_timings(true);  // bound the in-flight list
+  }
+  if (!capturing) {
+    if (order_ev_ == nullptr) ck(cudaEventCreateWithFlags(&order_ev_, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaEventRecord(order_ev_, s), "cudaEventRecord");
+    last_stream_ = s;
+    have_last_ = true;
   }
   stats_.launches += 1;
   const int64_t sub_b = L.sub_bytes;

@@ -10,9 +10,11 @@
 // made through an owned ProcessGroupNCCL (reference
 // cpp/src/process_group_lowbit.cc:67-70, :254-255, :292, :304).
 //
-// Calls on one LowBitComm must be stream-ordered (like an NCCL communicator):
-// every rank issues the same sequence of collectives, each on a stream that
-// orders it after the previous one.
+// Every rank must issue the same sequence of collectives on one LowBitComm
+// (like an NCCL communicator).  Launches from the host may use different
+// streams: a launch on a stream other than the previous launch's waits for
+// the previous launch's completion event first, so two streams never run
+// launches of one communicator at the same time.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -171,6 +173,10 @@ class LowBitComm {
   std::vector<cudaEvent_t> event_pool_;
   cudaEvent_t take_event();
   void collect_timings(bool wait);
+  // Completion event of the last host-issued (not captured) launch and its stream.
+  cudaEvent_t order_ev_ = nullptr;
+  cudaStream_t last_stream_ = nullptr;
+  bool have_last_ = false;
 };
 
 }  // namespace bitscom_b200

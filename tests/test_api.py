@@ -188,3 +188,76 @@ def test_error_feedback_residual_persists(fake_dist, monkeypatch):
     assert r.abs().sum() > 0
     g.all_reduce(t.clone(), ef_key="bucket0")
     assert not torch.equal(r, g._residuals["bucket0"])
+
+
+@pytest.mark.parametrize("use_key", [False, True])
+def test_error_feedback_checkpoint_resume_is_bit_identical(fake_dist, monkeypatch, use_key):
+    """A LowBitGroup restored from state_dict() continues exactly like the
+    uninterrupted run: residuals come back under their ef_key, or by order
+    of first use for tensors all-reduced without a key (new tensor objects
+    in the resumed process)."""
+    monkeypatch.setattr("bitscom_b200.api.dist.get_world_size", lambda group=None: 2)
+    torch.manual_seed(0)
+    grads = [[torch.randn(257), torch.randn(64)] for _ in range(4)]
+    kw = {"bitwidth": 2, "process_group": object(), "error_feedback": True, "stochastic_rounding": True}
+
+    def run(group, steps, bufs):
+        outs = []
+        for step in steps:
+            for i, buf in enumerate(bufs):
+                buf.copy_(grads[step][i])
+                group.all_reduce(buf, ef_key=(f"b{i}" if use_key else None))
+                outs.append(buf.clone())
+        return outs
+
+    full = LowBitGroup(**kw)
+    exp = run(full, range(4), [torch.empty(257), torch.empty(64)])
+    first = LowBitGroup(**kw)
+    got = run(first, range(2), [torch.empty(257), torch.empty(64)])
+    ck = first.state_dict()
+    resumed = LowBitGroup(**kw)
+    resumed.load_state_dict(ck)
+    got += run(resumed, range(2, 4), [torch.empty(257), torch.empty(64)])  # new buffers
+    assert len(got) == len(exp)
+    for a, b in zip(got, exp):
+        assert torch.equal(a, b)
+    assert resumed.state_dict()["calls"] == full.state_dict()["calls"]
+
+
+def test_hook_residuals_follow_bucket_parameters():
+    """Hook residuals are keyed by bucket index and parameter signature: a
+    rebuilt bucket with the same size but another parameter order starts from
+    zero (and the stale residual of that index is dropped); a checkpoint
+    restores residuals under the same keys."""
+    from bitscom_b200.parallel.hooks import LowBitHookState
+
+    params = [torch.nn.Parameter(torch.zeros(3)), torch.nn.Parameter(torch.zeros(3)), torch.nn.Parameter(torch.zeros(4))]
+
+    class Bucket:
+        def __init__(self, idx, ps):
+            self._i, self._p = idx, ps
+
+        def index(self):
+            return self._i
+
+        def parameters(self):
+            return self._p
+
+    s = LowBitHookState()
+    s.set_parameter_order(params)
+    b0 = Bucket(0, [params[0], params[1]])
+    buf = torch.zeros(6)
+    r = s.residual(0, buf, s.bucket_signature(b0))
+    r.fill_(1.0)
+    assert s.bucket_signature(b0) == (0, 1)
+    assert torch.equal(s.residual(0, buf, s.bucket_signature(b0)), torch.ones(6))
+    b0r = Bucket(0, [params[1], params[0]])  # rebuilt: same size, other order
+    r2 = s.residual(0, buf, s.bucket_signature(b0r))
+    assert torch.equal(r2, torch.zeros(6)) and len(s.residuals) == 1
+    r2.fill_(2.0)
+    t = LowBitHookState()
+    t.set_parameter_order(params)
+    t.load_state_dict(s.state_dict())
+    assert torch.equal(t.residual(0, buf, t.bucket_signature(b0r)), torch.full((6,), 2.0))
+    u = LowBitHookState()  # no parameter order: shapes stand in for indices
+    assert u.bucket_signature(b0) == ((3,), (3,))

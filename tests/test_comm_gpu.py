@@ -381,3 +381,28 @@ def test_sign_1bit_reduce_scatter_all_gather(comm):
     torch.cuda.synchronize()
     assert torch.equal(out.cpu(), emu.reduce_scatter([x], 1, fmt="sign")[0])
     assert torch.equal(g.cpu(), emu.all_gather([x], 1, fmt="sign"))
+
+
+def test_launches_on_two_streams_are_ordered():
+    """One communicator used from two streams (a DDP hook's comm stream and a
+    LowBitGroup call on the current stream): each launch waits for the
+    previous one, so the shared workspace and counters are never used by two
+    launches at once; every result is bit-exact against the model."""
+    c = Communicator.create_local(0, workspace_bytes=64 << 20)
+    side = torch.cuda.Stream()
+    cur = torch.cuda.current_stream()
+    xs = [_x(4_000_000 if i % 2 == 0 else 50_001, seed=100 + i) for i in range(6)]
+    rs = [torch.randn(x.numel()) * 1e-4 for x in xs]
+    ts = [x.cuda() for x in xs]
+    rgs = [r.cuda() for r in rs]
+    side.wait_stream(cur)
+    for i, (t, rg) in enumerate(zip(ts, rgs)):
+        with torch.cuda.stream(side if i % 2 == 0 else cur):
+            c.all_reduce(t, bits=4, residual=rg, algo="twoshot")
+    cur.wait_stream(side)
+    torch.cuda.synchronize()
+    c.check()
+    for x, r, t, rg in zip(xs, rs, ts, rgs):
+        exp, res = emu.allreduce_two_shot([x], 4, residuals=[r])
+        assert torch.equal(t.cpu(), exp)
+        assert torch.equal(rg.cpu(), res[0])

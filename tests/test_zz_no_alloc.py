@@ -33,6 +33,8 @@ def lib():
     so.bitscom_noalloc_scratch_bytes.restype = ctypes.c_longlong
     so.bitscom_noalloc_strerror.restype = ctypes.c_char_p
     so.bitscom_noalloc_strerror.argtypes = [ctypes.c_int]
+    so.bitscom_noalloc_status.restype = ctypes.c_int
+    so.bitscom_noalloc_status.argtypes = [ctypes.c_int]
     return so
 
 
@@ -45,10 +47,18 @@ def _call(lib, x, out, residual, bits, post_scale):
     return rc
 
 
-@pytest.mark.parametrize("dtype,bits", [(torch.float32, 4), (torch.bfloat16, 8), (torch.float32, 2)])
-def test_noalloc_matches_regular_entry_point_twice(lib, dtype, bits):
+@pytest.mark.parametrize("dtype,bits,n", [
+    (torch.float32, 4, 300001),
+    (torch.bfloat16, 8, 300001),
+    (torch.float32, 2, 300001),
+    (torch.float16, 4, 300001),
+    # at the scratch limit with the widest sub-chunks
+    (torch.float32, 12, 1 << 20),
+    (torch.float32, 16, 1 << 20),
+])
+def test_noalloc_matches_regular_entry_point_twice(lib, dtype, bits, n):
     torch.manual_seed(0)
-    n = 300001
+    assert n <= lib.bitscom_noalloc_max_elems()
     ref_comm = Communicator.create_local(0, workspace_bytes=64 << 20)
     res_ref = torch.randn(n, device="cuda") * 1e-4
     res_na = res_ref.clone()
@@ -60,6 +70,7 @@ def test_noalloc_matches_regular_entry_point_twice(lib, dtype, bits):
         rc = _call(lib, x, got, res_na, bits, 0.25)
         assert rc == 0, lib.bitscom_noalloc_strerror(rc)
         torch.cuda.synchronize()
+        assert lib.bitscom_noalloc_status(0) == 0
         assert torch.equal(got, exp), f"call {call}"
         assert torch.equal(res_na, res_ref), f"call {call}"
 

@@ -13,7 +13,12 @@ Timing: CUDA events on the launching stream around `iters` back-to-back
 calls after `warmup` calls, barrier + synchronize on both sides, max over
 ranks.  busBW = 2 (W-1)/W * fp32 bytes / time (the nccl-tests convention),
 so a low-bit all-reduce that moves fewer bytes shows as a higher
-fp32-equivalent bandwidth.  Rank 0 prints one JSON line per (impl, bits, size).
+fp32-equivalent bandwidth.  Rank 0 prints one JSON line per (impl, bits,
+algo, size); with ``--out FILE`` it also writes one JSON document with every
+row and the clock record (nvidia-smi samples of every GPU of the run, taken
+while the sweep ran: median SM clock under load, throttle reasons).
+``--algos oneshot twoshot`` times both fused algorithms at every size (the
+input of the tuning table); the default, ``auto``, times the automatic choice.
 """
 
 from __future__ import annotations
@@ -73,7 +78,8 @@ def main():
     p.add_argument("--residual-dtype", choices=["float32", "bfloat16"], default="float32",
                    help="element type of our error-feedback residual")
     p.add_argument("--no-sr", action="store_true")
-    p.add_argument("--algo", default="auto")
+    p.add_argument("--algos", nargs="+", default=["auto"], choices=["auto", "oneshot", "twoshot"])
+    p.add_argument("--out", default=None, help="rank 0 writes every row plus the clock record to this JSON file")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--max-ctas", type=int, default=0)
@@ -107,6 +113,10 @@ def main():
         ref_bitscom.init(bitwidth=args.bits[0], error_feedback=not args.no_ef)
         ref_pg = dist.new_group(backend="lowbit")
 
+    from bitscom_b200.utils.clocks import ClockSampler
+
+    sampler = ClockSampler(list(range(world)) if rank == 0 else [local]).__enter__()
+    rows = []
     sizes = []
     s = int(args.min_kb * 1024)
     while s <= int(args.max_mb * 2**20):
@@ -118,9 +128,10 @@ def main():
         x0 = gradient_like(n, rank, "cuda")
         buf = x0.clone()
         bus_factor = 2.0 * (world - 1) / world if world > 1 else 1.0
-        runs = [(impl, lag, spi) for impl in args.impls for lag in (args.lag if impl == "ours" else [None])
-                for spi in (args.spi if impl == "ours" else [None])]
-        for impl, lag, spi in runs:
+        runs = [(impl, lag, spi, algo) for impl in args.impls for lag in (args.lag if impl == "ours" else [None])
+                for spi in (args.spi if impl == "ours" else [None])
+                for algo in (args.algos if impl == "ours" else [None])]
+        for impl, lag, spi, algo in runs:
             if lag is not None:
                 comm.set_schedule_lag(lag)
             if spi is not None:
@@ -136,7 +147,7 @@ def main():
                         counter[0] += 1
                         comm.all_reduce(buf, bits=bits, fmt=fmt, residual=res,
                                         stochastic_rounding=not args.no_sr and fmt == "int",
-                                        offset=counter[0], algo=args.algo, max_ctas=args.max_ctas)
+                                        offset=counter[0], algo=algo, max_ctas=args.max_ctas)
                 elif impl == "reference_ef":
                     if fmt != "int" or bits != args.bits[0] or n % world:
                         continue
@@ -155,7 +166,7 @@ def main():
                 dist.all_reduce(exact)
                 buf.copy_(x0)
                 if impl == "ours":
-                    comm.all_reduce(buf, bits=bits, fmt=fmt, algo=args.algo)
+                    comm.all_reduce(buf, bits=bits, fmt=fmt, algo=algo)
                 else:
                     fn()
                 torch.cuda.synchronize()
@@ -164,17 +175,31 @@ def main():
                 if world > 1:
                     dist.all_reduce(rel_t, op=dist.ReduceOp.MAX)
                 if rank == 0:
-                    print(json.dumps({
+                    row = {
                         "impl": impl, "bits": bits, "fmt": fmt, "world": world, "bytes_fp32": n * 4,
+                        **({"algo": algo} if algo is not None else {}),
                         "ms": round(ms, 5), "busbw_fp32_equiv_GBs": round(bus_factor * n * 4 / (ms * 1e6), 2),
                         "algbw_GBs": round(n * 4 / (ms * 1e6), 2), "rel_err": float(rel_t.item()),
                         "ef": not args.no_ef and impl == "ours", "sr": not args.no_sr and impl != "nccl",
                         **({"residual_dtype": args.residual_dtype} if impl == "ours" and not args.no_ef else {}),
                         **({"lag": lag} if lag is not None and len(args.lag) > 1 else {}),
                         **({"spi": spi} if spi is not None and len(args.spi) > 1 else {}),
-                    }), flush=True)
+                    }
+                    rows.append(row)
+                    print(json.dumps(row), flush=True)
         del x0, buf
     dist.barrier()
+    sampler.__exit__(None, None, None)
+    if rank == 0 and args.out:
+        doc = {
+            "command": " ".join(sys.argv),
+            "world": world,
+            "timing": "CUDA events around iters back-to-back calls after warmup calls, max over ranks",
+            "clocks": sampler.summary(),
+            "rows": rows,
+        }
+        with open(args.out, "w", encoding="utf-8") as fh:
+            json.dump(doc, fh, indent=1)
     dist.destroy_process_group()
 
 

@@ -165,6 +165,16 @@ class Communicator:
         """Sub-chunks (8192 elements) per work item and completion flag: 0 automatic, 1..16 fixed."""
         self._c.set_sub_per_item(int(spi))
 
+    def set_kernel_variant(self, variant: str) -> None:
+        """Kernel organisation: "ws" (warp-specialised, a producer warp stages
+        data by bulk async copies; default) or "reg" (every warp loads and
+        waits itself).  Both produce identical bytes."""
+        self._c.set_kernel_variant({"ws": 0, "reg": 1}[variant])
+
+    @property
+    def kernel_variant(self) -> str:
+        return ("ws", "reg")[self._c.kernel_variant]
+
     def check_canaries(self) -> int:
         """Number of workspace guard regions that were overwritten (0 = none)."""
         return int(self._c.check_canaries())

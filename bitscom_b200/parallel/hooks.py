@@ -38,9 +38,14 @@ class LowBitHookState:
         stochastic_rounding: Philox stochastic rounding of the first quantisation.
         fp8: 8-bit buckets use the block-scaled E4M3 wire format.
         algo: "auto", "oneshot" or "twoshot".
-        max_ctas: CTAs of each fused launch (0 = two per SM).  The default, 32,
-            leaves most SMs to the backward kernels the launch overlaps with
-            (ResNet-18 DDP on 8 B200s: 275K samples/s at 32 CTAs, 261K at 296).
+        max_ctas: CTAs of each fused launch that overlaps backward (0 = a
+            full grid).  The default, 32, leaves most SMs to the backward
+            kernels the launch overlaps with (ResNet-18 DDP on 8 B200s: 275K
+            samples/s at 32 CTAs, 261K at a full grid).
+        last_bucket_ctas: CTAs of the launch of DDP's last bucket of an
+            iteration (``GradBucket.is_last()``), which runs after the final
+            backward kernel with nothing left to overlap: default 0, a full
+            grid.
         compress_single_rank: at world size 1 still run the (loopback) kernel,
             so a 1-GPU run applies exactly the quantisation an N-GPU run does.
         seed: Philox key of stochastic rounding.
@@ -60,6 +65,7 @@ class LowBitHookState:
         fp8: bool = False,
         algo: str = "auto",
         max_ctas: int = 32,
+        last_bucket_ctas: int = 0,
         compress_single_rank: bool = True,
         seed: int = 0x5EED,
         use_comm_stream: bool = True,
@@ -75,6 +81,7 @@ class LowBitHookState:
         self.fp8 = fp8 and bitwidth == 8
         self.algo = algo
         self.max_ctas = max_ctas
+        self.last_bucket_ctas = last_bucket_ctas
         self.compress_single_rank = compress_single_rank
         self.seed = int(seed)
         self.use_comm_stream = use_comm_stream
@@ -206,7 +213,7 @@ def lowbit_allreduce_hook(state: LowBitHookState, bucket: dist.GradBucket) -> to
             offset=state.calls,
             post_scale=1.0 / world,
             algo=state.algo,
-            max_ctas=state.max_ctas,
+            max_ctas=state.last_bucket_ctas if bucket.is_last() else state.max_ctas,
         )
         fut = torch.futures.Future(devices=[buf.device])
         fut.set_result(buf)

@@ -275,16 +275,33 @@ std::shared_ptr<LowBitComm> ProcessGroupLowBit::comm(int device) {
   return all_ok ? c : nullptr;
 }
 
-at::Tensor ProcessGroupLowBit::residual_for(const at::Tensor& key, int64_t numel, c10::Device dev) {
-  const int64_t k = static_cast<int64_t>(reinterpret_cast<uintptr_t>(key.unsafeGetTensorImpl()));
+at::Tensor ProcessGroupLowBit::residual_for(const at::Tensor& key, int64_t numel, c10::Device dev, ResidualKind kind) {
+  // All-reduce: keyed by the tensor (TensorImpl address), as the reference's
+  // residual cache (cpp/include/process_group_lowbit.h:117-119) keys it.
+  // Reduce-scatter / all-gather: keyed by (kind, buffer address), since
+  // sharded data parallel (e.g. FSDP2) passes a freshly created flat tensor
+  // over the same, allocator-reused buffer every step.
+  const int64_t k = kind == ResidualKind::kAllReduce
+                        ? static_cast<int64_t>(reinterpret_cast<uintptr_t>(key.unsafeGetTensorImpl()))
+                        : static_cast<int64_t>(reinterpret_cast<uintptr_t>(key.data_ptr()) ^
+                                               (static_cast<uint64_t>(kind) << 56));
   std::lock_guard<std::mutex> lk(mu_);
+  const uint64_t now = ++residual_clock_;
   auto it = residuals_.find(k);
-  if (it == residuals_.end() || it->second.numel() != numel || it->second.device() != dev) {
+  if (it == residuals_.end() || it->second.first.numel() != numel || it->second.first.device() != dev) {
+    if (it == residuals_.end() && residuals_.size() >= kMaxResiduals) {
+      // Bound the cache: drop the least recently used residual.
+      auto victim = residuals_.begin();
+      for (auto jt = residuals_.begin(); jt != residuals_.end(); ++jt)
+        if (jt->second.second < victim->second.second) victim = jt;
+      residuals_.erase(victim);
+    }
     auto r = at::zeros({numel}, at::TensorOptions().dtype(at::kFloat).device(dev));
-    residuals_[k] = r;
+    residuals_[k] = {r, now};
     return r;
   }
-  return it->second;
+  it->second.second = now;
+  return it->second.first;
 }
 
 int64_t ProcessGroupLowBit::residual_count() const { return static_cast<int64_t>(residuals_.size()); }
@@ -380,7 +397,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::allreduce_fused(std::vector<a
   for (auto& t : tensors) {
     at::Tensor buf = t.is_contiguous() ? t : t.contiguous();
     at::Tensor res;
-    if (options_.error_feedback) res = residual_for(t, buf.numel(), buf.device());
+    if (options_.error_feedback) res = residual_for(t, buf.numel(), buf.device(), ResidualKind::kAllReduce);
     const uint64_t offset = sr_calls_++;
     c->allreduce(buf.data_ptr(), buf.data_ptr(), res.defined() ? res.data_ptr<float>() : nullptr, buf.numel(),
                  dt_of(buf.scalar_type()), wire_bits(), wire_fmt(), options_.algo, options_.stochastic_rounding,
@@ -411,7 +428,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::allreduce_staged(std::vector<
     auto flat = t.reshape({-1}).to(at::kFloat);
     at::Tensor res;
     if (options_.error_feedback) {
-      res = residual_for(t, n, t.device());
+      res = residual_for(t, n, t.device(), ResidualKind::kAllReduce);
       flat = flat + res;
     }
     const int64_t pad = (W - n % W) % W;
@@ -479,7 +496,8 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::allreduce_coalesced(std::vect
 // ---------------------------------------------------------------------------
 // reduce-scatter / all-gather
 // ---------------------------------------------------------------------------
-c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::reduce_scatter_fused(at::Tensor& output, at::Tensor& input) {
+c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::reduce_scatter_fused(at::Tensor& output, at::Tensor& input,
+                                                                       float post_scale) {
   const int dev = input.device().index();
   auto c = comm(dev);
   auto cur = c10::cuda::getCurrentCUDAStream(dev);
@@ -492,10 +510,10 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::reduce_scatter_fused(at::Tens
   at::Tensor in = input.contiguous();
   at::Tensor out = output.is_contiguous() ? output : at::empty_like(output, at::MemoryFormat::Contiguous);
   at::Tensor res;
-  if (options_.error_feedback) res = residual_for(input, in.numel(), in.device());
+  if (options_.error_feedback) res = residual_for(in, in.numel(), in.device(), ResidualKind::kReduceScatter);
   c->reduce_scatter(in.data_ptr(), out.data_ptr(), res.defined() ? res.data_ptr<float>() : nullptr, out.numel(),
                     dt_of(in.scalar_type()), wire_bits(), wire_fmt(), options_.stochastic_rounding, options_.seed,
-                    sr_calls_++, 1.0f, cs.stream(), options_.max_ctas);
+                    sr_calls_++, post_scale, cs.stream(), options_.max_ctas);
   if (!out.is_same(output)) output.copy_(out);
   c10::cuda::CUDACachingAllocator::recordStream(in.storage().data_ptr(), cs);
   c10::cuda::CUDACachingAllocator::recordStream(output.storage().data_ptr(), cs);
@@ -521,7 +539,7 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::allgather_fused(at::Tensor& o
   at::Tensor in = input.contiguous();
   at::Tensor out = output.is_contiguous() ? output : at::empty_like(output, at::MemoryFormat::Contiguous);
   at::Tensor res;
-  if (options_.error_feedback) res = residual_for(input, in.numel(), in.device());
+  if (options_.error_feedback) res = residual_for(in, in.numel(), in.device(), ResidualKind::kAllGather);
   c->all_gather(in.data_ptr(), out.data_ptr(), res.defined() ? res.data_ptr<float>() : nullptr, in.numel(),
                 dt_of(in.scalar_type()), wire_bits(), wire_fmt(), options_.stochastic_rounding, options_.seed,
                 sr_calls_++, cs.stream(), options_.max_ctas);
@@ -544,12 +562,10 @@ c10::intrusive_ptr<c10d::Work> ProcessGroupLowBit::_reduce_scatter_base(at::Tens
   if (sum_like && use_lowbit_gather() && input.is_cuda() && fused_dtype(input) &&
       input.numel() == output.numel() * getSize() && comm(input.device().index()) != nullptr) {
     surface_errors();
-    auto w = reduce_scatter_fused(output, input);
-    if (opts.reduceOp == c10d::ReduceOp::AVG) {
-      c10::cuda::CUDAStreamGuard g(comm_stream(input.device().index()));
-      output.div_(getSize());
-    }
-    return w;
+    // AVG: the kernel scales its fp32 sums by 1/W before the output store, so
+    // the Work completes after the averaged values are written.
+    const float post = opts.reduceOp == c10d::ReduceOp::AVG ? 1.0f / static_cast<float>(getSize()) : 1.0f;
+    return reduce_scatter_fused(output, input, post);
   }
   ++forwarded_calls_;
   return inner(input)->_reduce_scatter_base(output, input, opts);

@@ -168,12 +168,13 @@ class ProcessGroupLowBit : public c10d::Backend {
   c10::intrusive_ptr<c10d::Backend> inner(const at::Tensor& t) const;
   c10::intrusive_ptr<c10d::Backend> inner_any() const;
   c10::cuda::CUDAStream comm_stream(int device);
-  at::Tensor residual_for(const at::Tensor& key, int64_t numel, c10::Device dev);
+  enum class ResidualKind : int { kAllReduce = 0, kReduceScatter = 1, kAllGather = 2 };
+  at::Tensor residual_for(const at::Tensor& key, int64_t numel, c10::Device dev, ResidualKind kind);
   void surface_errors();
 
   c10::intrusive_ptr<c10d::Work> allreduce_fused(std::vector<at::Tensor>& tensors);
   c10::intrusive_ptr<c10d::Work> allreduce_staged(std::vector<at::Tensor>& tensors);
-  c10::intrusive_ptr<c10d::Work> reduce_scatter_fused(at::Tensor& output, at::Tensor& input);
+  c10::intrusive_ptr<c10d::Work> reduce_scatter_fused(at::Tensor& output, at::Tensor& input, float post_scale);
   c10::intrusive_ptr<c10d::Work> allgather_fused(at::Tensor& output, at::Tensor& input);
 
   c10::intrusive_ptr<c10d::Store> store_;
@@ -183,7 +184,11 @@ class ProcessGroupLowBit : public c10d::Backend {
   std::unordered_map<int, std::shared_ptr<LowBitComm>> comms_;
   std::unordered_map<int, bool> p2p_ok_;
   std::unordered_map<int, c10::cuda::CUDAStream> streams_;
-  std::unordered_map<int64_t, at::Tensor> residuals_;  // keyed by TensorImpl address (reference parity)
+  // Error-feedback residuals with their last use (see residual_for for the
+  // keys); at most kMaxResiduals, least recently used dropped first.
+  static constexpr size_t kMaxResiduals = 1024;
+  std::unordered_map<int64_t, std::pair<at::Tensor, uint64_t>> residuals_;
+  uint64_t residual_clock_ = 0;
   std::vector<c10::intrusive_ptr<WorkLowBit>> recent_;  // for early error surfacing
   uint64_t sr_calls_ = 0;
   int comm_generation_ = 0;

@@ -315,6 +315,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("set_schedule_lag", &LowBitComm::set_schedule_lag)
       .def("device_epoch", &LowBitComm::device_epoch)
       .def("set_sub_per_item", &LowBitComm::set_sub_per_item)
+      .def("set_kernel_variant", &LowBitComm::set_kernel_variant)
+      .def_property_readonly("kernel_variant", &LowBitComm::kernel_variant)
+      .def("set_ws_smem_budget", &LowBitComm::set_ws_smem_budget)
       .def("set_oneshot_max_bytes", &LowBitComm::set_oneshot_max_bytes)
       .def("oneshot_max_bytes", &LowBitComm::oneshot_max_bytes)
       .def("check_canaries", &LowBitComm::check_canaries)

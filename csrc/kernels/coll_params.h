@@ -94,7 +94,24 @@ struct CollParams {
   // offset is `offset + epoch`, so replays draw fresh stochastic rounding.
   uint32_t* epoch_ctr;
   int offset_from_epoch;
+
+  // Warp-specialised kernel (lowbit_coll_ws_kernel): shared-memory ring of
+  // `stages` stages of `stage_bytes` each, filled by bulk async copies.  Zero
+  // stages selects the register-only kernel.  p2_bulk: the owner phase's W
+  // packed source sub-chunks fit in one stage and are staged too.
+  int stages;
+  int p2_bulk;
+  int64_t stage_bytes;
 };
+
+// Warp-specialised kernel geometry: 8 consumer warps (one 1024-element block
+// each per sub-chunk) and one producer warp; a fixed header (mbarriers, work
+// descriptors) precedes the stage ring in dynamic shared memory.
+constexpr int kWsConsumerWarps = 8;
+constexpr int kWsThreads = (kWsConsumerWarps + 1) * 32;
+constexpr int kWsDescSlots = 4;
+constexpr int kWsMaxStages = 8;
+constexpr int kWsHeaderBytes = 1024;
 
 // Work items per chunk in each phase of a collective (phase 1: encode and
 // push; phase 2: owner reduce; phase 3: decode a peer's reduced chunk).

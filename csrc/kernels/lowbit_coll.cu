@@ -41,12 +41,14 @@
 //   [8 x fp32 scales][8 x 128*bits bytes payload].
 // Payload words are interleaved across lanes in 16-byte vectors so every
 // store/load instruction of a warp covers a contiguous span.
+#include "bulk_async.cuh"
 #include "coll_params.h"
 #include "common.cuh"
 #include "launchers.h"
 
 #include <cuda_fp8.h>
 
+#include <atomic>
 #include <stdexcept>
 #include <string>
 
@@ -595,6 +597,536 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Warp-specialised kernel.
+//
+// Same work items, schedule, wire format and arithmetic as lowbit_coll_kernel
+// (so both produce identical bytes), reorganised so no warp that computes
+// ever waits on a peer or on a CTA-wide barrier:
+//
+//   producer warp (one elected lane): claims tickets, performs the bounded
+//     waits on peer completion flags (owner-reduce and decode items), then
+//     stages each sub-chunk's data into a ring of shared-memory stages with
+//     1-D bulk async copies from this GPU's own memory (cp.async.bulk, TMA
+//     engine) -- the gradient and residual sub-chunks of encode items, the W
+//     packed source sub-chunks of owner-reduce items (when they fit a stage),
+//     the packed sub-chunk of decode items -- and hands the item to the
+//     consumers through a small ring of work descriptors;
+//   8 consumer warps (one 1024-element block each per sub-chunk): take the
+//     next descriptor, read each stage from shared memory (or, for a partial
+//     or unaligned sub-chunk, straight from global memory), release the stage
+//     and compute/store as before.  The last warp to finish an item (counted
+//     with a CTA-scope acquire-release atomic instead of a CTA barrier)
+//     releases the item's completion flag(s) over NVLink.
+//
+// Stages and descriptors are tracked with mbarriers (full: producer arrival
+// plus transaction bytes; empty: one arrival per consumer warp).  The
+// producer runs up to `stages` sub-chunks ahead, so HBM reads stay in flight
+// while the consumers encode, and peer-flag latency hides behind the
+// consumers' work on earlier items.
+//
+// Deadlock freedom is the ticket argument of the register kernel: the only
+// waits on other CTAs or ranks are the producer's flag waits, each on items
+// of strictly earlier tickets; consumers wait only on their own producer,
+// which never waits on its own consumers except for ring space, which they
+// free without waiting on anything else.
+//
+// Every wait (flags, mbarriers) is bounded by %globaltimer; on expiry the
+// thread records kStatusTimeout, raises the launch's abort flag, and the CTA
+// drains: consumers stop, the producer waits (bounded) for the bulk copies it
+// issued and every thread returns normally.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct SmemIO;
+
+template <>
+struct SmemIO<float> {
+  __device__ __forceinline__ static void load4(const float* p, float (&o)[4]) {
+    const uint4 v = lds_v4(p);
+    o[0] = __uint_as_float(v.x); o[1] = __uint_as_float(v.y); o[2] = __uint_as_float(v.z); o[3] = __uint_as_float(v.w);
+  }
+};
+
+template <>
+struct SmemIO<__nv_bfloat16> {
+  __device__ __forceinline__ static void load4(const __nv_bfloat16* p, float (&o)[4]) {
+    const uint2 t = lds_v2(p);
+    const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.x));
+    const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.y));
+    o[0] = fa.x; o[1] = fa.y; o[2] = fb.x; o[3] = fb.y;
+  }
+};
+
+template <>
+struct SmemIO<__half> {
+  __device__ __forceinline__ static void load4(const __half* p, float (&o)[4]) {
+    const uint2 t = lds_v2(p);
+    const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&t.x));
+    const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&t.y));
+    o[0] = fa.x; o[1] = fa.y; o[2] = fb.x; o[3] = fb.y;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void load_block_smem(const T* blk, int lane, float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float t[4];
+    SmemIO<T>::load4(blk + (k * 32 + lane) * 4, t);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) v[k * 4 + m] = t[m];
+  }
+}
+
+template <int B>
+__device__ __forceinline__ void get_words_smem(const uint8_t* sub, int blk, int lane, uint32_t (&w)[B]) {
+  const uint8_t* pay = sub + kHeaderBytes + blk * 128 * B;
+  if constexpr (B % 4 == 0) {
+#pragma unroll
+    for (int r = 0; r < B / 4; ++r) {
+      const uint4 t = lds_v4(pay + (r * 32 + lane) * 16);
+      w[4 * r] = t.x; w[4 * r + 1] = t.y; w[4 * r + 2] = t.z; w[4 * r + 3] = t.w;
+    }
+  } else if constexpr (B == 2) {
+    const uint2 t = lds_v2(pay + lane * 8);
+    w[0] = t.x; w[1] = t.y;
+  } else {
+    w[0] = lds_u32(pay + lane * 4);
+  }
+}
+
+__device__ __forceinline__ float get_scale_smem(const uint8_t* sub, int blk) {
+  return __uint_as_float(lds_u32(sub + blk * 4));
+}
+
+// Bounded mbarrier wait (one thread).  Returns false on timeout (after
+// recording it and raising the abort flag) or when the launch was aborted.
+__device__ bool ws_wait(const CollParams& p, uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 15u) == 0u) {
+      if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        *reinterpret_cast<volatile uint32_t*>(p.status) = kStatusTimeout;
+        atomicExch(p.abort_flag, 1u);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Warp-wide form: lane 0 waits, the result is broadcast, and __syncwarp
+// orders the other lanes' later reads after lane 0's acquire.
+__device__ __forceinline__ bool ws_warp_wait(const CollParams& p, uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                             int lane) {
+  int ok = 1;
+  if (lane == 0) ok = ws_wait(p, bar, parity, limit_ns) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+template <typename T, typename R, int B, int FMT>
+__global__ void __launch_bounds__(kWsThreads, 1) lowbit_coll_ws_kernel(const __grid_constant__ CollParams p) {
+  using C = Codec<B, FMT>;
+  extern __shared__ __align__(128) uint8_t ws_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(ws_smem);
+  uint64_t* empty = full + kWsMaxStages;
+  uint64_t* dfull = empty + kWsMaxStages;
+  uint64_t* dempty = dfull + kWsDescSlots;
+  int64_t* d_item = reinterpret_cast<int64_t*>(dempty + kWsDescSlots);
+  int* d_ok = reinterpret_cast<int*>(d_item + kWsDescSlots);
+  uint32_t* d_cnt = reinterpret_cast<uint32_t*>(d_ok + kWsDescSlots);
+  uint32_t* s_epoch = d_cnt + kWsDescSlots;
+  uint8_t* stage_base = ws_smem + kWsHeaderBytes;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int W = p.world;
+  const int me = p.rank;
+  const int64_t IS = p.n_items_slot;
+  const int spi = p.sub_per_item;
+  const bool vec_in = (reinterpret_cast<uintptr_t>(p.in) & 15u) == 0;
+  const bool vec_out = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
+  const bool vec_res = (reinterpret_cast<uintptr_t>(p.residual) & 15u) == 0;
+  const bool has_res = p.residual != nullptr;
+  const T* in = static_cast<const T*>(p.in);
+  R* residual = static_cast<R*>(p.residual);
+  T* out = static_cast<T*>(p.out);
+  const bool skip_signals = p.fault_skip != nullptr && *p.fault_skip != 0u;  // test hook
+  const int S = p.stages;
+  const int64_t SB = p.stage_bytes;
+  const int64_t SUBB = p.sub_bytes;
+  const uint64_t wait_ns = p.timeout_ns;
+
+  int a1, a2, a3;
+  coll_phase_items(p.op, W, &a1, &a2, &a3);
+  const int64_t n1 = a1 * IS, n2 = a2 * IS, n3 = a3 * IS;
+  const int64_t total = n1 + n2 + n3;
+  const bool bcast1 = (p.op == kAllReduceOneShot || p.op == kAllGather);
+
+  auto shard_lim = [&](int d) -> int64_t {
+    const int64_t rest = p.n - static_cast<int64_t>(d) * p.in_stride;
+    return rest < p.shard_valid ? rest : p.shard_valid;
+  };
+  // Encode items: destination rank, input base and valid length.
+  auto enc_geom = [&](int64_t item, int64_t& c, int& dst, int64_t& base, int64_t& lim) {
+    c = bcast1 ? item : item / W;
+    dst = bcast1 ? me : (me + 1 + static_cast<int>(item % W)) % W;
+    base = bcast1 ? 0 : static_cast<int64_t>(dst) * p.in_stride;
+    lim = bcast1 ? p.n : shard_lim(dst);
+  };
+  // Whether an encode sub-chunk is staged by bulk copy (identical decision in
+  // producer and consumers): aligned input (and residual) and a full sub-chunk.
+  auto bulk1 = [&](int64_t base, int64_t lim, int64_t sub) -> bool {
+    if (!vec_in || ((base * static_cast<int64_t>(sizeof(T))) & 15) != 0) return false;
+    if (has_res && (!vec_res || ((base * static_cast<int64_t>(sizeof(R))) & 15) != 0)) return false;
+    return (sub + 1) * kSubElems <= lim;
+  };
+  auto nsub_of = [&](int64_t c) -> int {
+    const int64_t r = p.n_sub - c * spi;
+    return static_cast<int>(r < spi ? r : spi);
+  };
+
+  if (threadIdx.x == 0) {
+    uint32_t e = p.epoch;
+    if (p.epoch_ctr != nullptr) {
+      e = *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u;
+      if (e == 0u) e = 1u;
+    }
+    *s_epoch = e;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWsConsumerWarps);
+    }
+    for (int i = 0; i < kWsDescSlots; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], kWsConsumerWarps);
+      d_cnt[i] = 0u;
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  const uint32_t epoch = *s_epoch;
+  const int par = p.epoch_ctr != nullptr ? static_cast<int>(epoch & 1u) : p.parity;
+  const uint64_t offset = p.offset + (p.offset_from_epoch ? static_cast<uint64_t>(epoch) : 0ull);
+
+  if (warp == kWsConsumerWarps) {
+    // ============================================================ producer
+    if (lane == 0) {
+      uint32_t dseq = 0, sseq = 0;
+      while (true) {
+        const uint32_t t = atomicAdd(p.ticket, 1u);
+        int64_t item = coll_schedule_item(p.op, W, IS, p.lag, static_cast<int64_t>(t));
+        if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) item = total;
+        const int slot = static_cast<int>(dseq % kWsDescSlots);
+        if (!ws_wait(p, &dempty[slot], ((dseq / kWsDescSlots) & 1u) ^ 1u, wait_ns)) break;
+        bool ok = true;
+        int kind = 0, src = 0;
+        int64_t c = 0;
+        if (item < total) {
+          if (item < n1) {
+            kind = 1;
+            c = bcast1 ? item : item / W;
+          } else if (item < n1 + n2) {
+            kind = 2;
+            c = item - n1;
+            for (int s = 0; s < W && ok; ++s) ok = wait_epoch(p, epoch, rs_flag(p, par, me, s, c));
+          } else {
+            kind = 3;
+            const int64_t k3 = item - n1 - n2;
+            c = k3 / (W - 1);
+            src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
+            ok = wait_epoch(p, epoch, ag_flag(p, par, me, src, c));
+          }
+          // Peers' stores, acquired through the flags, are read next by bulk
+          // copies (async proxy).
+          if (kind >= 2 && ok) fence_proxy_async_global();
+        }
+        d_item[slot] = item;
+        d_ok[slot] = ok ? 1 : 0;
+        mbar_arrive(&dfull[slot]);
+        ++dseq;
+        if (item >= total || !ok) break;
+
+        int64_t base = 0, lim = 0, c1 = 0;
+        int dst = 0;
+        if (kind == 1) enc_geom(item, c1, dst, base, lim);
+        const int64_t sub0 = c * spi;
+        const int nsub = nsub_of(c);
+        bool alive = true;
+        for (int g = 0; g < nsub; ++g) {
+          const int64_t sub = sub0 + g;
+          const int st = static_cast<int>(sseq % S);
+          if (!ws_wait(p, &empty[st], ((sseq / S) & 1u) ^ 1u, wait_ns)) {
+            alive = false;
+            break;
+          }
+          uint8_t* sbuf = stage_base + st * SB;
+          if (kind == 1) {
+            if (bulk1(base, lim, sub)) {
+              const uint32_t xb = kSubElems * static_cast<uint32_t>(sizeof(T));
+              const uint32_t rb = has_res ? kSubElems * static_cast<uint32_t>(sizeof(R)) : 0u;
+              mbar_arrive_expect_tx(&full[st], xb + rb);
+              bulk_g2s(sbuf, in + base + sub * kSubElems, xb, &full[st]);
+              if (has_res) bulk_g2s(sbuf + xb, residual + base + sub * kSubElems, rb, &full[st]);
+            } else {
+              mbar_arrive(&full[st]);
+            }
+          } else if (kind == 2) {
+            if (p.p2_bulk) {
+              mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(W * SUBB));
+              for (int s = 0; s < W; ++s)
+                bulk_g2s(sbuf + s * SUBB, rs_sub(p, par, me, s, sub), static_cast<uint32_t>(SUBB), &full[st]);
+            } else {
+              mbar_arrive(&full[st]);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(SUBB));
+            bulk_g2s(sbuf, ag_sub(p, par, me, src, sub), static_cast<uint32_t>(SUBB), &full[st]);
+          }
+          ++sseq;
+        }
+        if (!alive) break;
+      }
+      // Drain: every bulk copy this CTA issued has landed before it exits
+      // (bounded; the copies read local memory and complete in microseconds).
+      const uint32_t armed = sseq < static_cast<uint32_t>(S) ? sseq : static_cast<uint32_t>(S);
+      for (uint32_t i = sseq - armed; i < sseq; ++i) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[i % S], (i / S) & 1u)) {
+          if (globaltimer_ns() - t0 > wait_ns) break;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ============================================================ consumers
+    uint32_t dseq = 0, sseq = 0;
+    while (true) {
+      const int slot = static_cast<int>(dseq % kWsDescSlots);
+      if (!ws_warp_wait(p, &dfull[slot], (dseq / kWsDescSlots) & 1u, 2 * wait_ns, lane)) break;
+      const int64_t item = d_item[slot];
+      const int ok = d_ok[slot];
+      if (item >= total || !ok) break;
+      bool alive = true;
+      int kind, dst = 0;
+      int64_t c;
+      if (item < n1) {
+        // ---------------------------------------------------------- encode
+        kind = 1;
+        int64_t base, lim;
+        enc_geom(item, c, dst, base, lim);
+        const bool vx = vec_in && ((base * static_cast<int64_t>(sizeof(T))) & 15) == 0;
+        const bool vr = vec_res && ((base * static_cast<int64_t>(sizeof(R))) & 15) == 0;
+        const int nsub = nsub_of(c);
+        for (int g = 0; g < nsub; ++g) {
+          const int64_t sub = c * spi + g;
+          const int st = static_cast<int>(sseq % S);
+          if (!ws_warp_wait(p, &full[st], (sseq / S) & 1u, 2 * wait_ns, lane)) {
+            alive = false;
+            break;
+          }
+          const int64_t off = sub * kSubElems + warp * kBlockElems;
+          const uint8_t* sbuf = stage_base + st * SB;
+          float v[32];
+          if (bulk1(base, lim, sub)) {
+            load_block_smem<T>(reinterpret_cast<const T*>(sbuf) + warp * kBlockElems, lane, v);
+            if (has_res) {
+              float r[32];
+              load_block_smem<R>(reinterpret_cast<const R*>(sbuf + kSubElems * sizeof(T)) + warp * kBlockElems, lane, r);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
+            }
+          } else {
+            load_block<T>(in, base + off, base + lim, vx, lane, v);
+            if (has_res) {
+              float r[32];
+              load_block<R>(residual, base + off, base + lim, vr, lane, r);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);
+          ++sseq;
+          uint32_t w[B];
+          float scale;
+          if (has_res) {
+            scale = encode_block<B, FMT, kKeepResidual>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
+                                                        1u + 4u * me, p.seed, offset, w);
+            store_block<R>(residual, base + off, base + lim, vr, lane, v);
+          } else {
+            scale = encode_block<B, FMT, kKeepInput>(v, p.stochastic != 0, static_cast<uint64_t>((base + off) >> 2) + lane,
+                                                     1u + 4u * me, p.seed, offset, w);
+          }
+          if (!bcast1) {
+            uint8_t* d = rs_sub(p, par, dst, me, sub);
+            put_words<B>(d, warp, lane, w);
+            if (lane == 0) put_scale(d, warp, scale);
+          } else {
+            for (int k = 0; k < W; ++k) {
+              const int d = (me + 1 + k) % W;
+              uint8_t* dp = (p.op == kAllGather) ? ag_sub(p, par, d, me, sub) : rs_sub(p, par, d, me, sub);
+              put_words<B>(dp, warp, lane, w);
+              if (lane == 0) put_scale(dp, warp, scale);
+            }
+            if (p.op == kAllGather) {
+              float o[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] = C::decode(get_code<B>(w, j), scale);
+              const bool va = vec_out && ((static_cast<int64_t>(me) * p.out_stride * static_cast<int64_t>(sizeof(T))) & 15) == 0;
+              store_block<T>(out + static_cast<int64_t>(me) * p.out_stride, off, p.n, va, lane, o);
+            }
+          }
+        }
+      } else if (item < n1 + n2) {
+        // ---------------------------------------------------- owner reduce
+        kind = 2;
+        c = item - n1;
+        const int nsub = nsub_of(c);
+        for (int g = 0; g < nsub; ++g) {
+          const int64_t sub = c * spi + g;
+          const int st = static_cast<int>(sseq % S);
+          if (!ws_warp_wait(p, &full[st], (sseq / S) & 1u, 2 * wait_ns, lane)) {
+            alive = false;
+            break;
+          }
+          const uint8_t* sbuf = stage_base + st * SB;
+          float acc[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+          constexpr int G = kSrcBatch<B>;
+          for (int s0 = 0; s0 < W; s0 += G) {
+            uint32_t wv[G][B];
+            float sc[G];
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+              if (s0 + u < W) {
+                if (p.p2_bulk) {
+                  const uint8_t* src = sbuf + (s0 + u) * SUBB;
+                  get_words_smem<B>(src, warp, lane, wv[u]);
+                  sc[u] = get_scale_smem(src, warp);
+                } else {
+                  const uint8_t* src = rs_sub(p, par, me, s0 + u, sub);
+                  get_words<B>(src, warp, lane, wv[u]);
+                  sc[u] = get_scale(src, warp);
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+              if (s0 + u < W) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], C::decode(get_code<B>(wv[u], j), sc[u]));
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);
+          ++sseq;
+          const int64_t off = sub * kSubElems + warp * kBlockElems;
+          if (p.op == kAllReduceTwoShot) {
+            const int64_t elem_base = static_cast<int64_t>(me) * p.shard_len + off;
+            uint32_t w[B];
+            const float scale = encode_block<B, FMT, kKeepDequant>(acc, p.stochastic2 != 0,
+                                                                   static_cast<uint64_t>(elem_base >> 2) + lane,
+                                                                   2u + 4u * me, p.seed, offset, w);
+            for (int k = 0; k < W; ++k) {
+              const int d = (me + 1 + k) % W;
+              uint8_t* dp = ag_sub(p, par, d, me, sub);
+              put_words<B>(dp, warp, lane, w);
+              if (lane == 0) put_scale(dp, warp, scale);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = __fmul_rn(acc[j], p.post_scale);
+            store_block<T>(out, elem_base, p.n, vec_out, lane, acc);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = __fmul_rn(acc[j], p.post_scale);
+            store_block<T>(out, off, p.op == kReduceScatter ? shard_lim(me) : p.n, vec_out, lane, acc);
+          }
+        }
+      } else {
+        // ---------------------------------------------------------- decode
+        kind = 3;
+        const int64_t k3 = item - n1 - n2;
+        c = k3 / (W - 1);
+        const int src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
+        const bool ag = p.op == kAllGather;
+        const int64_t obase = ag ? static_cast<int64_t>(src) * p.out_stride : static_cast<int64_t>(src) * p.shard_len;
+        const bool vo = vec_out && ((ag ? obase * static_cast<int64_t>(sizeof(T)) : 0) & 15) == 0;
+        const int nsub = nsub_of(c);
+        for (int g = 0; g < nsub; ++g) {
+          const int64_t sub = c * spi + g;
+          const int st = static_cast<int>(sseq % S);
+          if (!ws_warp_wait(p, &full[st], (sseq / S) & 1u, 2 * wait_ns, lane)) {
+            alive = false;
+            break;
+          }
+          const uint8_t* sbuf = stage_base + st * SB;
+          uint32_t w[B];
+          get_words_smem<B>(sbuf, warp, lane, w);
+          const float sc = get_scale_smem(sbuf, warp);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[st]);
+          ++sseq;
+          float o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __fmul_rn(C::decode(get_code<B>(w, j), sc), p.post_scale);
+          const int64_t off = sub * kSubElems + warp * kBlockElems;
+          if (ag) store_block<T>(out + obase, off, p.n, vo, lane, o);
+          else store_block<T>(out, obase + off, p.n, vec_out, lane, o);
+        }
+      }
+      if (!alive) break;
+      // Item done in this warp; the last of the 8 warps releases its flags.
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = (atom_add_acq_rel_cta(&d_cnt[slot], 1u) == kWsConsumerWarps - 1) ? 1 : 0;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      __syncwarp();
+      if (last) {
+        if (lane == 0) d_cnt[slot] = 0u;
+        if (!skip_signals) {
+          if (kind == 1) {
+            if (!bcast1) {
+              if (lane == 0) st_release_sys(rs_flag(p, par, dst, me, c), epoch);
+            } else if (lane < W) {
+              const int d = (me + 1 + lane) % W;
+              st_release_sys((p.op == kAllGather) ? ag_flag(p, par, d, me, c) : rs_flag(p, par, d, me, c), epoch);
+            }
+          } else if (kind == 2 && p.op == kAllReduceTwoShot && lane < W) {
+            const int d = (me + 1 + lane) % W;
+            st_release_sys(ag_flag(p, par, d, me, c), epoch);
+          }
+        }
+        __syncwarp();
+      }
+      if (lane == 0) mbar_arrive(&dempty[slot]);
+      ++dseq;
+    }
+  }
+
+  // Exit bookkeeping: the last CTA out resets the launch-local counters.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.done, 1u);
+    if (prev == gridDim.x - 1) {
+      if (p.epoch_ctr != nullptr) *p.epoch_ctr = epoch;
+      *p.ticket = 0u;
+      *p.done = 0u;
+      *p.abort_flag = 0u;
+      __threadfence();
+    }
+  }
+}
+
 template <typename F>
 void dispatch_bits_fmt(int bits, int fmt, F&& f) {
   if (fmt == kFmtE4M3) {
@@ -619,17 +1151,52 @@ void dispatch_bits_fmt(int bits, int fmt, F&& f) {
   }
 }
 
+// Opt-in to the dynamic shared memory of the warp-specialised kernel, once
+// per instantiation and device (the template parameters make the static
+// per kernel instantiation).
+template <typename T, typename R, int B, int F>
+cudaError_t ws_prepare(int bytes) {
+  auto kernel = lowbit_coll_ws_kernel<T, R, B, F>;
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  int optin = 0;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  if (bytes > optin) return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+template <typename T, typename R, int B, int F>
+cudaError_t launch_one(const CollParams& p, int grid, cudaStream_t s) {
+  if (p.stages > 0) {
+    if (p.stages > kWsMaxStages || p.stage_bytes <= 0 || (p.stage_bytes & 127) != 0) return cudaErrorInvalidValue;
+    const int smem = kWsHeaderBytes + static_cast<int>(p.stages * p.stage_bytes);
+    const cudaError_t e = ws_prepare<T, R, B, F>(smem);
+    if (e != cudaSuccess) return e;
+    lowbit_coll_ws_kernel<T, R, B, F><<<grid, kWsThreads, smem, s>>>(p);
+  } else {
+    lowbit_coll_kernel<T, R, B, F><<<grid, kThreads, 0, s>>>(p);
+  }
+  return cudaGetLastError();
+}
+
 template <int B, int F, typename T>
-void launch_res(const CollParams& p, int grid, cudaStream_t s) {
-  if (p.res_dtype == kBF16) lowbit_coll_kernel<T, __nv_bfloat16, B, F><<<grid, kThreads, 0, s>>>(p);
-  else lowbit_coll_kernel<T, float, B, F><<<grid, kThreads, 0, s>>>(p);
+cudaError_t launch_res(const CollParams& p, int grid, cudaStream_t s) {
+  if (p.res_dtype == kBF16) return launch_one<T, __nv_bfloat16, B, F>(p, grid, s);
+  return launch_one<T, float, B, F>(p, grid, s);
 }
 
 template <int B, int F>
-void launch_typed(const CollParams& p, DType dt, int grid, cudaStream_t s) {
-  if (dt == kF32) launch_res<B, F, float>(p, grid, s);
-  else if (dt == kBF16) launch_res<B, F, __nv_bfloat16>(p, grid, s);
-  else launch_res<B, F, __half>(p, grid, s);
+cudaError_t launch_typed(const CollParams& p, DType dt, int grid, cudaStream_t s) {
+  if (dt == kF32) return launch_res<B, F, float>(p, grid, s);
+  if (dt == kBF16) return launch_res<B, F, __nv_bfloat16>(p, grid, s);
+  return launch_res<B, F, __half>(p, grid, s);
 }
 
 }  // namespace
@@ -642,8 +1209,8 @@ void lowbit_coll(const CollParams& p, DType dt, int bits, int grid, cudaStream_t
   if (p.world < 1 || p.world > kMaxRanks) throw std::runtime_error("bitscom: world size must be 1..8");
   if (p.res_dtype != kF32 && p.res_dtype != kBF16) throw std::runtime_error("bitscom: residual must be fp32 or bf16");
   if (dt != kF32 && dt != kBF16 && dt != kF16) throw std::runtime_error("bitscom: unsupported dtype");
-  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) { launch_typed<decltype(bc)::value, decltype(fc)::value>(p, dt, grid, s); });
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) { e = launch_typed<decltype(bc)::value, decltype(fc)::value>(p, dt, grid, s); });
   if (e != cudaSuccess) throw std::runtime_error(std::string("lowbit_coll_kernel: ") + cudaGetErrorString(e));
 }
 
@@ -658,8 +1225,9 @@ cudaError_t lowbit_coll_nothrow(const CollParams& p, DType dt, int bits, int gri
   if (bits != 1 && bits != 2 && bits != 4 && bits != 8 && bits != 12 && bits != 16) return cudaErrorInvalidValue;
   if (dt != kF32 && dt != kBF16 && dt != kF16) return cudaErrorInvalidValue;
   if (p.res_dtype != kF32 && p.res_dtype != kBF16) return cudaErrorInvalidValue;
-  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) { launch_typed<decltype(bc)::value, decltype(fc)::value>(p, dt, grid, s); });
-  return cudaGetLastError();
+  cudaError_t e = cudaSuccess;
+  dispatch_bits_fmt(bits, p.fmt, [&](auto bc, auto fc) { e = launch_typed<decltype(bc)::value, decltype(fc)::value>(p, dt, grid, s); });
+  return e;
 }
 
 }  // namespace launch

@@ -78,6 +78,13 @@ LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
   if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) set_timeout_ms(std::atof(t));
   if (const char* t = std::getenv("BITSCOM_SCHED_LAG")) sched_lag_ = std::atoll(t);
   if (const char* t = std::getenv("BITSCOM_SUB_PER_ITEM")) spi_override_ = std::atoi(t);
+  if (const char* t = std::getenv("BITSCOM_KERNEL")) {
+    const std::string k(t);
+    if (k == "reg") kernel_variant_ = kKernelRegister;
+    else if (k == "ws" || k.empty()) kernel_variant_ = kKernelWarpSpecialised;
+    else throw std::runtime_error("bitscom: BITSCOM_KERNEL must be ws or reg");
+  }
+  if (const char* t = std::getenv("BITSCOM_WS_SMEM_KB")) ws_smem_budget_ = std::max<int64_t>(32, std::atoll(t)) << 10;
   if (const char* t = std::getenv("BITSCOM_ALGO")) {
     const std::string a(t);
     if (a == "oneshot") algo_override_ = kAlgoOneShot;
@@ -269,8 +276,11 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   p.shard_valid = shard_valid;
   p.out_stride = out_stride > 0 ? out_stride : n;
   p.n_sub = n_sub;
-  // Two 256-thread CTAs fit per SM (the kernel is bounded to 128 registers).
-  const int resident = 2 * sm_count_;
+  // Warp-specialised kernel: one 288-thread CTA per SM (its stage ring takes
+  // most of the shared memory).  Register kernel: two 256-thread CTAs per SM
+  // (bounded to 128 registers).
+  const bool ws = kernel_variant_ == kKernelWarpSpecialised;
+  const int resident = ws ? sm_count_ : 2 * sm_count_;
   const int grid_cap = std::max(1, max_ctas > 0 ? std::min(max_ctas, resident) : resident);
   // Items: enough for ~8 per CTA in phase 1, at most 16 sub-chunks each.
   const int64_t phase1_units = (op == kAllReduceTwoShot || op == kReduceScatter) ? world_ * n_sub : n_sub;
@@ -315,6 +325,24 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   if (cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusActive) p.offset_from_epoch = 1;
   p.status = status_dev_;
   p.timeout_ns = timeout_ns_;
+  if (ws) {
+    // Stage = the largest unit staged at once: an encode sub-chunk (8192
+    // inputs + residuals), a decode sub-chunk (one packed sub-chunk) and, when
+    // it fits in 64 KB, the owner's W packed source sub-chunks.
+    const int64_t esz = dt == kF32 ? 4 : 2;
+    const int64_t rsz = residual ? (residual.dt == kF32 ? 4 : 2) : 0;
+    int64_t sb = std::max<int64_t>(kSubElems * (esz + rsz), L.sub_bytes);
+    const int64_t p2 = world_ * L.sub_bytes;
+    const bool p2_bulk = p2 <= std::max<int64_t>(sb, 64ll << 10);
+    if (p2_bulk) sb = std::max(sb, p2);
+    sb = (sb + 127) & ~int64_t(127);
+    const int64_t stages = std::min<int64_t>(kWsMaxStages, ws_smem_budget_ / sb);
+    if (stages >= 2) {
+      p.stages = static_cast<int>(stages);
+      p.stage_bytes = sb;
+      p.p2_bulk = p2_bulk ? 1 : 0;
+    }
+  }
 
   int a1, a2, a3;
   coll_phase_items(op, world_, &a1, &a2, &a3);

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -29,6 +30,10 @@
 namespace bitscom_b200 {
 
 enum Algo : int { kAlgoAuto = 0, kAlgoTwoShot = 1, kAlgoOneShot = 2 };
+
+// Kernel organisation: warp-specialised with a bulk-copy stage ring (default)
+// or the register-only kernel (every warp loads, computes and waits itself).
+enum KernelVariant : int { kKernelWarpSpecialised = 0, kKernelRegister = 1 };
 
 // Error-feedback residual: fp32 or bf16 elements (null = no error feedback).
 // A bf16 residual halves the residual's HBM traffic (read + write per
@@ -115,6 +120,18 @@ class LowBitComm {
   // automatic choice.
   void set_oneshot_max_bytes(int64_t b) { oneshot_max_bytes_ = b < 0 ? 0 : b; }
   int64_t oneshot_max_bytes() const { return oneshot_max_bytes_; }
+  // Kernel organisation (KernelVariant); env BITSCOM_KERNEL=ws|reg sets the
+  // initial value.  Both variants produce identical bytes.
+  void set_kernel_variant(int v) {
+    if (v != kKernelWarpSpecialised && v != kKernelRegister) throw std::runtime_error("bitscom: kernel variant must be 0 (ws) or 1 (reg)");
+    kernel_variant_ = v;
+  }
+  int kernel_variant() const { return kernel_variant_; }
+  // Shared memory of the warp-specialised kernel's stage ring (bytes; env
+  // BITSCOM_WS_SMEM_KB).  At least two stages must fit, else the register
+  // kernel runs.
+  void set_ws_smem_budget(int64_t bytes) { ws_smem_budget_ = bytes < (32 << 10) ? (32 << 10) : bytes; }
+  int64_t ws_smem_budget() const { return ws_smem_budget_; }
   // Number of workspace guard regions whose bytes changed since creation
   // (0 = none).  Synchronises the device.
   int check_canaries() const;
@@ -163,6 +180,8 @@ class LowBitComm {
   int spi_override_ = 0;
   int64_t oneshot_max_bytes_ = 512ll << 10;
   int algo_override_ = kAlgoAuto;
+  int kernel_variant_ = kKernelWarpSpecialised;
+  int64_t ws_smem_budget_ = 200ll << 10;
   std::vector<int64_t> canary_offsets() const;
   int sm_count_ = 148;
   bool ready_ = false;

@@ -406,3 +406,66 @@ def test_launches_on_two_streams_are_ordered():
         exp, res = emu.allreduce_two_shot([x], 4, residuals=[r])
         assert torch.equal(t.cpu(), exp)
         assert torch.equal(rg.cpu(), res[0])
+
+
+@pytest.fixture(scope="module")
+def variant_pair():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    ws = Communicator.create_local(0, workspace_bytes=64 << 20)
+    reg = Communicator.create_local(0, workspace_bytes=64 << 20)
+    reg.set_kernel_variant("reg")
+    assert ws.kernel_variant == "ws" and reg.kernel_variant == "reg"
+    return ws, reg
+
+
+@pytest.mark.parametrize("op", ["twoshot", "oneshot", "reduce_scatter", "all_gather"])
+@pytest.mark.parametrize("bits,fmt", [(1, "int"), (1, "sign"), (2, "int"), (4, "int"), (8, "e4m3"), (12, "int"), (16, "int")])
+@pytest.mark.parametrize("dtype,res_dtype", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                             (torch.float16, None)])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_warp_specialised_kernel_matches_register_kernel(variant_pair, op, bits, fmt, dtype, res_dtype, offset):
+    """The warp-specialised kernel (bulk-copy stage ring) and the register
+    kernel produce identical outputs and residuals; offset 1 makes every
+    pointer unaligned, so the staged path falls back to direct loads."""
+    ws, reg = variant_pair
+    n = 3 * 8192 * 5 + 4097
+    base = _x(n + offset, seed=bits * 7 + offset, dtype=dtype).cuda()
+    results = []
+    for c in (ws, reg):
+        x = base[offset:]
+        r = None
+        if res_dtype is not None:
+            r = (torch.randn(n + offset, generator=torch.Generator().manual_seed(3)) * 1e-4).to(res_dtype).cuda()[offset:]
+        if op in ("twoshot", "oneshot"):
+            out = torch.empty(n + offset, dtype=dtype, device="cuda")[offset:]
+            c.all_reduce(x, out=out, bits=bits, fmt=fmt, residual=r, algo=op, post_scale=0.5,
+                         stochastic_rounding=(fmt == "int"), seed=7, offset=3)
+        elif op == "reduce_scatter":
+            out = torch.empty(n + offset, dtype=dtype, device="cuda")[offset:]
+            c.reduce_scatter(out, x, bits=bits, fmt=fmt, residual=r, stochastic_rounding=(fmt == "int"), seed=7)
+        else:
+            out = torch.empty(n + offset, dtype=dtype, device="cuda")[offset:]
+            c.all_gather(out, x, bits=bits, fmt=fmt, residual=r)
+        torch.cuda.synchronize()
+        c.check()
+        results.append((out.cpu(), None if r is None else r.cpu()))
+    assert torch.equal(results[0][0], results[1][0])
+    if res_dtype is not None:
+        assert torch.equal(results[0][1], results[1][1])
+
+
+def test_warp_specialised_kernel_large_twoshot_matches_model(variant_pair):
+    """Large sizes stage many sub-chunks per CTA: compare a multi-item launch
+    against the CPU model."""
+    ws, _ = variant_pair
+    n = 8192 * 600 + 123
+    x = _x(n, seed=42)
+    r = torch.randn(n) * 1e-4
+    t, rg = x.cuda(), r.cuda()
+    ws.all_reduce(t, bits=4, residual=rg, algo="twoshot")
+    torch.cuda.synchronize()
+    ws.check()
+    exp, res = emu.allreduce_two_shot([x], 4, residuals=[r])
+    assert torch.equal(t.cpu(), exp)
+    assert torch.equal(rg.cpu(), res[0])

@@ -160,7 +160,7 @@ def test_lowbit_backend_fused_path():
         assert st2["fused_calls"] == 3 and torch.equal(b, torch.ones(4))
 
 
-def _w_ddp(rank, world):
+def _w_ddp(rank, world, lowbit=True):
     import bitscom_b200 as bitscom
     from bitscom_b200.models import resnet18_cifar
 
@@ -168,7 +168,7 @@ def _w_ddp(rank, world):
     torch.manual_seed(0)
     model = resnet18_cifar(10).cuda()
     ddp = torch.nn.parallel.DistributedDataParallel(model, device_ids=[rank], bucket_cap_mb=5)
-    state = bitscom.register_lowbit_hook(ddp, bitwidth=4, error_feedback=True)
+    state = bitscom.register_lowbit_hook(ddp, bitwidth=4, error_feedback=True) if lowbit else None
     opt = torch.optim.SGD(ddp.parameters(), lr=0.05, momentum=0.9)
     g = torch.Generator(device="cuda").manual_seed(rank)
     for _ in range(5):
@@ -181,16 +181,27 @@ def _w_ddp(rank, world):
         opt.zero_grad()
     torch.cuda.synchronize()
     p = torch.cat([q.detach().float().view(-1) for q in model.parameters()]).cpu()
-    launches = sum(c.stats()["launches"] for c in state._comms.values() if c is not None)
+    launches = sum(c.stats()["launches"] for c in state._comms.values() if c is not None) if lowbit else 0
     dist.destroy_process_group()
     return p, launches
 
 
 def test_ddp_hook_replicas_stay_identical():
+    """4-bit EF DDP: replicas bit-identical, and the training trajectory
+    tracks fp32 DDP (the parameter update of 5 steps points the same way)."""
     _need(2)
     res = run_ranks(_w_ddp, 2, env=ENV, timeout=300)
+    fp = run_ranks(_w_ddp, 2, (False,), env=ENV, timeout=300)
     assert torch.equal(res[0][0], res[1][0])
     assert res[0][1] > 5
+    torch.manual_seed(0)
+    from bitscom_b200.models import resnet18_cifar
+
+    p0 = torch.cat([q.detach().float().view(-1) for q in resnet18_cifar(10).parameters()])
+    d_lb, d_fp = res[0][0] - p0, fp[0][0] - p0
+    cos = float(torch.dot(d_lb, d_fp) / (d_lb.norm() * d_fp.norm()))
+    assert cos > 0.9, cos
+    assert float((d_lb - d_fp).norm() / d_fp.norm()) < 0.5
 
 
 def _w_timeout(rank, world):
@@ -251,11 +262,22 @@ def _w_pipeline(rank, world):
 
 
 def test_pipeline_a_on_gpus():
+    """Pipeline-A with singleton local groups (every rank a leader, the
+    reference's own test topology): the dual-stream schedule runs every chunk
+    through the inter stage, the fused one-shot 4-bit all-reduce of that
+    chunk (30000 elements, 15 KB packed: below the one-shot threshold), so the
+    result equals the block model chunk by chunk, bit for bit, on every rank."""
     _need(2)
-    res = run_ranks(_w_pipeline, 2, env=ENV)
-    y, exp, ga = res[0]
+    world = 2
+    res = run_ranks(_w_pipeline, world, env=ENV)
+    xs = [(torch.linspace(-1.0, 1.0, 100003) + r * 0.01) for r in range(world)]
+    exp = torch.cat([
+        emu.allreduce_one_shot([x[s:s + 30000] for x in xs], 4)[0] for s in range(0, 100003, 30000)
+    ])
+    y, fp, ga = res[0]
     assert torch.equal(ga[0], ga[1])
-    assert (y - exp).abs().max() / exp.abs().max() < 0.2
+    assert torch.equal(y, exp)
+    assert (y - fp).abs().max() / fp.abs().max() < 0.1  # and it tracks the fp32 sum
 
 
 def _w_sdp(rank, world):
@@ -329,3 +351,64 @@ def test_graph_replay_across_ranks_matches_model():
         exp, _ = emu.allreduce_one_shot([mid] * world, 8)
         for r in range(world):
             assert torch.equal(res[r][1][i], exp), (i, r)
+
+
+class _Scale(torch.nn.Module):
+    """y = x * w with a flat weight: the gradient of sum(y) is x exactly, so
+    the reduce-scatter input is known bit-for-bit; forward records the
+    unsharded weight FSDP2 all-gathered."""
+
+    def __init__(self, n):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.zeros(n))
+        self.seen = None
+
+    def forward(self, x):
+        self.seen = self.weight.detach().clone()
+        return x * self.weight
+
+
+def _w_fsdp2(rank, world, n):
+    import bitscom_b200 as bitscom
+    from torch.distributed.device_mesh import DeviceMesh
+    from torch.distributed.fsdp import fully_shard
+
+    bitscom.init(bitwidth=8, error_feedback=False, force_lowbit=True)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("lowbit", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    mesh = DeviceMesh.from_group(dist.group.WORLD, "cuda")
+    model = _Scale(n).cuda()
+    w0 = _x(n, 0, seed=21)  # the same full weight on every rank before sharding
+    with torch.no_grad():
+        model.weight.copy_(w0.cuda())
+    fully_shard(model, mesh=mesh)
+    x = _x(n, rank, seed=22).cuda()
+    loss = model(x).sum()
+    loss.backward()
+    torch.cuda.synchronize()
+    seen = model.seen.cpu()
+    grad_shard = model.weight.grad.to_local().cpu()
+    be = dist.group.WORLD._get_backend(torch.device("cuda"))
+    st = dict(be.stats())
+    dist.destroy_process_group()
+    return w0, x.cpu(), seen, grad_shard, st
+
+
+def test_fsdp2_step_on_lowbit_group_matches_model():
+    """FSDP2 (fully_shard) on a `lowbit` process group on GPUs: its parameter
+    all-gather and gradient reduce-scatter run the fused 8-bit kernels
+    (backend counters), and the unsharded weight and the averaged gradient
+    shard equal the wire model bit-for-bit on every rank."""
+    _need(2)
+    world, n = 2, 8192 * 6
+    res = run_ranks(_w_fsdp2, world, (n,), env=ENV, timeout=300)
+    w0 = res[0][0]
+    shard = n // world
+    exp_w = emu.all_gather([w0[r * shard:(r + 1) * shard] for r in range(world)], 8)
+    exp_g = emu.reduce_scatter([res[r][1] for r in range(world)], 8, post_scale=1.0 / world)
+    for r in range(world):
+        _, _, seen, grad_shard, st = res[r]
+        assert torch.equal(seen, exp_w), r
+        assert torch.equal(grad_shard, exp_g[r]), r
+        assert st["fused_calls"] >= 2, st  # at least one all-gather and one reduce-scatter

@@ -65,6 +65,9 @@ def create_backend(store, rank: int, size: int, timeout, bitwidth: int = 4, erro
     opts.max_ctas = int(cfg["max_ctas"])
     opts.seed = int(cfg["seed"])
     opts.blocking_wait = bool(cfg["blocking_wait"])
+    from .tuning import entries as _tuning_entries
+
+    opts.tuning = [list(e) for e in _tuning_entries(size)]
     if cfg["oneshot_max_bytes"] is None:
         from .tuning import oneshot_max_bytes
 

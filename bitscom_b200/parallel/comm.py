@@ -61,9 +61,11 @@ class Communicator:
     def __init__(self, native, group=None):
         self._c = native
         self.group = group
-        from ..tuning import oneshot_max_bytes
+        from ..tuning import entries, oneshot_max_bytes
 
         native.set_oneshot_max_bytes(oneshot_max_bytes(native.world))
+        for bits, fmt, one, ws in entries(native.world):
+            native.set_tuning(bits, fmt, one, ws)
 
     # ------------------------------------------------------------------ setup
     @classmethod
@@ -166,9 +168,9 @@ class Communicator:
         self._c.set_sub_per_item(int(spi))
 
     def set_kernel_variant(self, variant: str) -> None:
-        """Kernel organisation: "ws" (warp-specialised, a producer warp stages
-        data by bulk async copies; default) or "reg" (every warp loads and
-        waits itself).  Both produce identical bytes."""
+        """Kernel organisation: "reg" (every warp loads and waits itself;
+        default) or "ws" (warp-specialised: a producer warp waits on peers and
+        stages data by bulk async copies).  Both produce identical bytes."""
         self._c.set_kernel_variant({"ws": 0, "reg": 1}[variant])
 
     @property

@@ -49,8 +49,12 @@ class LowBitHookState:
         compress_single_rank: at world size 1 still run the (loopback) kernel,
             so a 1-GPU run applies exactly the quantisation an N-GPU run does.
         seed: Philox key of stochastic rounding.
-        residual_dtype: element type of the EF residuals (torch.float32 or
-            torch.bfloat16; bf16 halves their HBM traffic inside the kernel).
+        residual_dtype: element type of the EF residuals (torch.bfloat16,
+            the default, or torch.float32).  bf16 halves the residual's HBM
+            traffic inside the kernel; measured with the collective's own
+            encode (``benchmarks/error_feedback_comparison.py --fused``), the
+            EF cumulative error after 160 steps is the same to three digits
+            at 2, 4 and 8 bits (4-bit: 0.01141 bf16 vs 0.01139 fp32).
         sign_1bit: with bitwidth 1, send sign codes with a mean-|x| block
             scale (error-feedback signSGD) instead of the reference's
             unsigned {0, 1} codes, which drop every negative value.
@@ -69,7 +73,7 @@ class LowBitHookState:
         compress_single_rank: bool = True,
         seed: int = 0x5EED,
         use_comm_stream: bool = True,
-        residual_dtype: torch.dtype = torch.float32,
+        residual_dtype: torch.dtype = torch.bfloat16,
         sign_1bit: bool = False,
     ):
         if bitwidth not in (1, 2, 4, 8, 12, 16):

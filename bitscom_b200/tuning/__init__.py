@@ -1,10 +1,18 @@
-"""Tuning table of the fused collectives (algorithm crossover by world size).
+"""Tuning table of the fused collectives.
 
 The table is a JSON file (``b200.json`` beside this module, or the file named
-by ``BITSCOM_TUNING_FILE``) with the largest packed message, in bytes per
-rank, for which the one-shot all-reduce is chosen automatically; larger
-messages use the two-shot form.  ``BITSCOM_ALGO=oneshot|twoshot`` overrides
-the automatic choice altogether (read by the native communicator).
+by ``BITSCOM_TUNING_FILE``) with
+
+* ``oneshot_max_packed_bytes``: per world size, the largest packed message,
+  in bytes per rank, for which the one-shot all-reduce is chosen
+  automatically (larger messages use the two-shot form);
+* ``entries``: per (world size, bitwidth, wire format) overrides measured on
+  the device: ``oneshot_max_packed_bytes`` and ``ws_min_packed_bytes`` (the
+  packed size from which the warp-specialised kernel runs instead of the
+  register kernel; -1 or absent: never).
+
+``BITSCOM_ALGO=oneshot|twoshot`` and ``BITSCOM_KERNEL=ws|reg`` override the
+automatic choices altogether (read by the native communicator).
 """
 
 from __future__ import annotations
@@ -37,3 +45,22 @@ def oneshot_max_bytes(world: int, path: Optional[str] = None) -> int:
     per_world = table.get("oneshot_max_packed_bytes", {})
     v = per_world.get(str(int(world)), table.get("default_oneshot_max_packed_bytes", FALLBACK_ONESHOT_MAX_BYTES))
     return int(v)
+
+
+FMTS = {"int": 0, "e4m3": 1, "sign": 2}
+
+
+def entries(world: int, path: Optional[str] = None):
+    """[(bits, fmt_code, oneshot_max_bytes, ws_min_bytes)] of the table's
+    per-format entries for ``world`` ranks (-1 = no value)."""
+    try:
+        table = load_table(path)
+    except (OSError, ValueError):
+        return []
+    out = []
+    for e in table.get("entries", []):
+        if int(e.get("world", -1)) != int(world):
+            continue
+        out.append((int(e["bits"]), FMTS[e.get("fmt", "int")], int(e.get("oneshot_max_packed_bytes", -1)),
+                    int(e.get("ws_min_packed_bytes", -1))))
+    return out

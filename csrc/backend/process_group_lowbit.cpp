@@ -225,6 +225,8 @@ std::shared_ptr<LowBitComm> ProcessGroupLowBit::comm(int device) {
     c = std::make_shared<LowBitComm>(R, W, device, ws);
     c->set_timeout_ms(static_cast<double>(options_.timeout.count()));
     c->set_oneshot_max_bytes(options_.oneshot_max_bytes);
+    for (const auto& e : options_.tuning)
+      if (e.size() == 4) c->set_tuning(static_cast<int>(e[0]), static_cast<int>(e[1]), e[2], e[3]);
     if (const char* t = std::getenv("BITSCOM_TIMEOUT_MS")) c->set_timeout_ms(std::atof(t));
   } catch (const std::exception& e) {
     err = e.what();
@@ -730,6 +732,7 @@ void register_backend_bindings(pybind11::module& m) {
       .def_readwrite("workspace_bytes", &LowBitOptions::workspace_bytes)
       .def_readwrite("max_ctas", &LowBitOptions::max_ctas)
       .def_readwrite("oneshot_max_bytes", &LowBitOptions::oneshot_max_bytes)
+      .def_readwrite("tuning", &LowBitOptions::tuning)
       .def_readwrite("seed", &LowBitOptions::seed)
       .def_readwrite("blocking_wait", &LowBitOptions::blocking_wait);
 

@@ -58,6 +58,8 @@ struct LowBitOptions {
   uint64_t seed = 0x5eed;
   bool blocking_wait = false;        // Work.wait() blocks the host and checks the kernel status
   int64_t oneshot_max_bytes = 512ll << 10;  // automatic algorithm: one-shot up to this packed size
+  // Tuning-table entries for this world size: {bits, fmt, oneshot_max_bytes, ws_min_bytes}.
+  std::vector<std::vector<int64_t>> tuning;
 };
 
 class WorkLowBit : public c10d::Work {

@@ -319,6 +319,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("kernel_variant", &LowBitComm::kernel_variant)
       .def("set_ws_smem_budget", &LowBitComm::set_ws_smem_budget)
       .def("set_oneshot_max_bytes", &LowBitComm::set_oneshot_max_bytes)
+      .def("set_tuning", &LowBitComm::set_tuning, py::arg("bits"), py::arg("fmt"), py::arg("oneshot_max_bytes"), py::arg("ws_min_bytes"))
       .def("oneshot_max_bytes", &LowBitComm::oneshot_max_bytes)
       .def("check_canaries", &LowBitComm::check_canaries)
       .def("sub_per_item", &LowBitComm::sub_per_item)

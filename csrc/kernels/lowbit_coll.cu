@@ -471,10 +471,13 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
     } else if (item < n1 + n2) {
       // ------------------------------------------------------------ phase 2
       const int64_t c = item - n1;
-      if (threadIdx.x == 0) {
-        bool ok = true;
-        for (int s = 0; s < W && ok; ++s) ok = wait_epoch(p, epoch, rs_flag(p, par, me, s, c));
-        s_ok[cur] = ok ? 1 : 0;
+      if (warp == 0) {
+        // Lane s waits for source s: the W flag round trips overlap instead
+        // of running one after another.
+        const bool ok = lane < W ? wait_epoch(p, epoch, rs_flag(p, par, me, lane, c)) : true;
+        __syncwarp();
+        const bool all = __all_sync(0xffffffffu, ok);
+        if (lane == 0) s_ok[cur] = all ? 1 : 0;
       }
       __syncthreads();
       if (!s_ok[cur]) break;
@@ -817,84 +820,106 @@ __global__ void __launch_bounds__(kWsThreads, 1) lowbit_coll_ws_kernel(const __g
 
   if (warp == kWsConsumerWarps) {
     // ============================================================ producer
-    if (lane == 0) {
-      uint32_t dseq = 0, sseq = 0;
-      while (true) {
+    // The whole warp runs the loop in step (every branch below is uniform);
+    // lane 0 claims tickets and issues the mbarrier operations and bulk
+    // copies, lanes 0..W-1 wait on the W source flags of an owner item in
+    // parallel.
+    uint32_t dseq = 0, sseq = 0;
+    while (true) {
+      int64_t item = 0;
+      if (lane == 0) {
         const uint32_t t = atomicAdd(p.ticket, 1u);
-        int64_t item = coll_schedule_item(p.op, W, IS, p.lag, static_cast<int64_t>(t));
+        item = coll_schedule_item(p.op, W, IS, p.lag, static_cast<int64_t>(t));
         if (*reinterpret_cast<volatile uint32_t*>(p.abort_flag) != 0u) item = total;
-        const int slot = static_cast<int>(dseq % kWsDescSlots);
-        if (!ws_wait(p, &dempty[slot], ((dseq / kWsDescSlots) & 1u) ^ 1u, wait_ns)) break;
-        bool ok = true;
-        int kind = 0, src = 0;
-        int64_t c = 0;
-        if (item < total) {
-          if (item < n1) {
-            kind = 1;
-            c = bcast1 ? item : item / W;
-          } else if (item < n1 + n2) {
-            kind = 2;
-            c = item - n1;
-            for (int s = 0; s < W && ok; ++s) ok = wait_epoch(p, epoch, rs_flag(p, par, me, s, c));
-          } else {
-            kind = 3;
-            const int64_t k3 = item - n1 - n2;
-            c = k3 / (W - 1);
-            src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
-            ok = wait_epoch(p, epoch, ag_flag(p, par, me, src, c));
-          }
-          // Peers' stores, acquired through the flags, are read next by bulk
-          // copies (async proxy).
-          if (kind >= 2 && ok) fence_proxy_async_global();
+      }
+      item = __shfl_sync(0xffffffffu, item, 0);
+      const int slot = static_cast<int>(dseq % kWsDescSlots);
+      int free_ok = 1;
+      if (lane == 0) free_ok = ws_wait(p, &dempty[slot], ((dseq / kWsDescSlots) & 1u) ^ 1u, wait_ns) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, free_ok, 0)) break;
+      bool ok = true;
+      int kind = 0, src = 0;
+      int64_t c = 0;
+      if (item < total) {
+        if (item < n1) {
+          kind = 1;
+          c = bcast1 ? item : item / W;
+        } else if (item < n1 + n2) {
+          kind = 2;
+          c = item - n1;
+          ok = lane < W ? wait_epoch(p, epoch, rs_flag(p, par, me, lane, c)) : true;
+          __syncwarp();
+          ok = __all_sync(0xffffffffu, ok);
+        } else {
+          kind = 3;
+          const int64_t k3 = item - n1 - n2;
+          c = k3 / (W - 1);
+          src = (me + 1 + static_cast<int>(k3 % (W - 1))) % W;
+          int okl = 1;
+          if (lane == 0) okl = wait_epoch(p, epoch, ag_flag(p, par, me, src, c)) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
         }
+        // Peers' stores, acquired through the flags, are read next by bulk
+        // copies (async proxy).
+        if (kind >= 2 && ok) fence_proxy_async_global();
+      }
+      if (lane == 0) {
         d_item[slot] = item;
         d_ok[slot] = ok ? 1 : 0;
         mbar_arrive(&dfull[slot]);
-        ++dseq;
-        if (item >= total || !ok) break;
-
-        int64_t base = 0, lim = 0, c1 = 0;
-        int dst = 0;
-        if (kind == 1) enc_geom(item, c1, dst, base, lim);
-        const int64_t sub0 = c * spi;
-        const int nsub = nsub_of(c);
-        bool alive = true;
-        for (int g = 0; g < nsub; ++g) {
-          const int64_t sub = sub0 + g;
-          const int st = static_cast<int>(sseq % S);
-          if (!ws_wait(p, &empty[st], ((sseq / S) & 1u) ^ 1u, wait_ns)) {
-            alive = false;
-            break;
-          }
-          uint8_t* sbuf = stage_base + st * SB;
-          if (kind == 1) {
-            if (bulk1(base, lim, sub)) {
-              const uint32_t xb = kSubElems * static_cast<uint32_t>(sizeof(T));
-              const uint32_t rb = has_res ? kSubElems * static_cast<uint32_t>(sizeof(R)) : 0u;
-              mbar_arrive_expect_tx(&full[st], xb + rb);
-              bulk_g2s(sbuf, in + base + sub * kSubElems, xb, &full[st]);
-              if (has_res) bulk_g2s(sbuf + xb, residual + base + sub * kSubElems, rb, &full[st]);
-            } else {
-              mbar_arrive(&full[st]);
-            }
-          } else if (kind == 2) {
-            if (p.p2_bulk) {
-              mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(W * SUBB));
-              for (int s = 0; s < W; ++s)
-                bulk_g2s(sbuf + s * SUBB, rs_sub(p, par, me, s, sub), static_cast<uint32_t>(SUBB), &full[st]);
-            } else {
-              mbar_arrive(&full[st]);
-            }
-          } else {
-            mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(SUBB));
-            bulk_g2s(sbuf, ag_sub(p, par, me, src, sub), static_cast<uint32_t>(SUBB), &full[st]);
-          }
-          ++sseq;
-        }
-        if (!alive) break;
       }
-      // Drain: every bulk copy this CTA issued has landed before it exits
-      // (bounded; the copies read local memory and complete in microseconds).
+      ++dseq;
+      if (item >= total || !ok) break;
+
+      int64_t base = 0, lim = 0, c1 = 0;
+      int dst = 0;
+      if (kind == 1) enc_geom(item, c1, dst, base, lim);
+      const int64_t sub0 = c * spi;
+      const int nsub = nsub_of(c);
+      bool alive = true;
+      for (int g = 0; g < nsub; ++g) {
+        const int64_t sub = sub0 + g;
+        const int st = static_cast<int>(sseq % S);
+        int room = 1;
+        if (lane == 0) {
+          room = ws_wait(p, &empty[st], ((sseq / S) & 1u) ^ 1u, wait_ns) ? 1 : 0;
+          if (room) {
+            uint8_t* sbuf = stage_base + st * SB;
+            if (kind == 1) {
+              if (bulk1(base, lim, sub)) {
+                const uint32_t xb = kSubElems * static_cast<uint32_t>(sizeof(T));
+                const uint32_t rb = has_res ? kSubElems * static_cast<uint32_t>(sizeof(R)) : 0u;
+                mbar_arrive_expect_tx(&full[st], xb + rb);
+                bulk_g2s(sbuf, in + base + sub * kSubElems, xb, &full[st]);
+                if (has_res) bulk_g2s(sbuf + xb, residual + base + sub * kSubElems, rb, &full[st]);
+              } else {
+                mbar_arrive(&full[st]);
+              }
+            } else if (kind == 2) {
+              if (p.p2_bulk) {
+                mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(W * SUBB));
+                for (int s = 0; s < W; ++s)
+                  bulk_g2s(sbuf + s * SUBB, rs_sub(p, par, me, s, sub), static_cast<uint32_t>(SUBB), &full[st]);
+              } else {
+                mbar_arrive(&full[st]);
+              }
+            } else {
+              mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(SUBB));
+              bulk_g2s(sbuf, ag_sub(p, par, me, src, sub), static_cast<uint32_t>(SUBB), &full[st]);
+            }
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, room, 0)) {
+          alive = false;
+          break;
+        }
+        ++sseq;
+      }
+      if (!alive) break;
+    }
+    // Drain: every bulk copy this CTA issued has landed before it exits
+    // (bounded; the copies read local memory and complete in microseconds).
+    if (lane == 0) {
       const uint32_t armed = sseq < static_cast<uint32_t>(S) ? sseq : static_cast<uint32_t>(S);
       for (uint32_t i = sseq - armed; i < sseq; ++i) {
         const uint64_t t0 = globaltimer_ns();
@@ -1085,6 +1110,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) lowbit_coll_ws_kernel(const __g
       }
       if (!alive) break;
       // Item done in this warp; the last of the 8 warps releases its flags.
+      // Every lane first fences its own peer stores at system scope, so the
+      // release below never depends on another warp's stores still being in
+      // flight over NVLink.
+      if ((kind == 1 || (kind == 2 && p.op == kAllReduceTwoShot)) && !skip_signals) __threadfence_system();
       __syncwarp();
       int last = 0;
       if (lane == 0) last = (atom_add_acq_rel_cta(&d_cnt[slot], 1u) == kWsConsumerWarps - 1) ? 1 : 0;

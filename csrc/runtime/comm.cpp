@@ -80,9 +80,10 @@ LowBitComm::LowBitComm(int rank, int world, int device, int64_t workspace_bytes)
   if (const char* t = std::getenv("BITSCOM_SUB_PER_ITEM")) spi_override_ = std::atoi(t);
   if (const char* t = std::getenv("BITSCOM_KERNEL")) {
     const std::string k(t);
-    if (k == "reg") kernel_variant_ = kKernelRegister;
-    else if (k == "ws" || k.empty()) kernel_variant_ = kKernelWarpSpecialised;
-    else throw std::runtime_error("bitscom: BITSCOM_KERNEL must be ws or reg");
+    if (k == "reg") kernel_variant_ = kKernelRegister, kernel_forced_ = true;
+    else if (k == "ws") kernel_variant_ = kKernelWarpSpecialised, kernel_forced_ = true;
+    else if (k.empty() || k == "auto") kernel_forced_ = false;
+    else throw std::runtime_error("bitscom: BITSCOM_KERNEL must be auto, ws or reg");
   }
   if (const char* t = std::getenv("BITSCOM_WS_SMEM_KB")) ws_smem_budget_ = std::max<int64_t>(32, std::atoll(t)) << 10;
   if (const char* t = std::getenv("BITSCOM_ALGO")) {
@@ -279,7 +280,8 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   // Warp-specialised kernel: one 288-thread CTA per SM (its stage ring takes
   // most of the shared memory).  Register kernel: two 256-thread CTAs per SM
   // (bounded to 128 registers).
-  const bool ws = kernel_variant_ == kKernelWarpSpecialised;
+  const int64_t packed_bytes = n * bits / 8;
+  const bool ws = kernel_for(bits, fmt, packed_bytes) == kKernelWarpSpecialised;
   const int resident = ws ? sm_count_ : 2 * sm_count_;
   const int grid_cap = std::max(1, max_ctas > 0 ? std::min(max_ctas, resident) : resident);
   // Items: enough for ~8 per CTA in phase 1, at most 16 sub-chunks each.
@@ -389,6 +391,13 @@ void LowBitComm::launch(int op, const void* in, void* out, ResidualBuf residual,
   else stats_.wire_bytes += static_cast<uint64_t>(world_ - 1) * n_sub * sub_b;
 }
 
+int LowBitComm::kernel_for(int bits, int fmt, int64_t packed_bytes) const {
+  if (kernel_forced_) return kernel_variant_;
+  const int64_t t = (bits >= 1 && bits <= 16 && fmt >= 0 && fmt <= 2) ? tune_ws_min_[fmt][bits] : -1;
+  if (t >= 0) return packed_bytes >= t ? kKernelWarpSpecialised : kKernelRegister;
+  return kernel_variant_;
+}
+
 void LowBitComm::allreduce(const void* in, void* out, ResidualBuf residual, int64_t n, DType dt, int bits,
                            int fmt, int algo, bool sr, bool sr_requant, uint64_t seed, uint64_t offset,
                            float post_scale, cudaStream_t s, int max_ctas) {
@@ -403,7 +412,8 @@ void LowBitComm::allreduce(const void* in, void* out, ResidualBuf residual, int6
     // dependent phases.  Measured crossover on B200 (4-bit, W=2 and W=8):
     // one-shot wins up to 512 KB packed (4 MB fp32), two-shot from 1 MB.
     const int64_t packed = n * bits / 8;
-    a = (world_ == 1 || packed <= oneshot_max_bytes_) ? kAlgoOneShot : kAlgoTwoShot;
+    const int64_t t = (bits >= 1 && bits <= 16 && fmt >= 0 && fmt <= 2) ? tune_oneshot_[fmt][bits] : -1;
+    a = (world_ == 1 || packed <= (t >= 0 ? t : oneshot_max_bytes_)) ? kAlgoOneShot : kAlgoTwoShot;
   }
   const int op = (a == kAlgoOneShot) ? kAllReduceOneShot : kAllReduceTwoShot;
   const int64_t cap = max_elems_per_launch(op, bits);

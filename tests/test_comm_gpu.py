@@ -413,6 +413,7 @@ def variant_pair():
     if not torch.cuda.is_available():
         pytest.skip("CUDA device required")
     ws = Communicator.create_local(0, workspace_bytes=64 << 20)
+    ws.set_kernel_variant("ws")
     reg = Communicator.create_local(0, workspace_bytes=64 << 20)
     reg.set_kernel_variant("reg")
     assert ws.kernel_variant == "ws" and reg.kernel_variant == "reg"

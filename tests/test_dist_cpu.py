@@ -282,7 +282,7 @@ def test_missing_rank_is_detected_by_timeout():
     assert res[0].startswith("raised")
 
 
-def _w_fsdp2(rank, world, backend):
+def _w_fsdp2(rank, world, backend, custom=False):
     import torch.nn as nn
     from torch.distributed.device_mesh import DeviceMesh
     from torch.distributed.fsdp import fully_shard
@@ -295,7 +295,13 @@ def _w_fsdp2(rank, world, backend):
     mesh = DeviceMesh.from_group(dist.group.WORLD, "cpu")
     torch.manual_seed(0)
     model = nn.Sequential(nn.Linear(64, 128), nn.ReLU(), nn.Linear(128, 10))
+    fully_shard(model[0], mesh=mesh)
     fully_shard(model, mesh=mesh)
+    comms = {}
+    if custom:
+        from bitscom_b200.parallel.fsdp2 import enable_lowbit_fsdp2
+
+        comms = enable_lowbit_fsdp2(model, bits=8)
     opt = torch.optim.SGD(model.parameters(), lr=0.1)
     g = torch.Generator().manual_seed(rank)
     losses = []
@@ -309,6 +315,8 @@ def _w_fsdp2(rank, world, backend):
     stats = {}
     if backend == "lowbit":
         stats = dict(dist.group.WORLD._get_backend(torch.device("cpu")).stats())
+    if custom:
+        stats = {"modules": sorted(comms), "fused": sum(a.fused_calls + r.fused_calls for a, r in comms.values())}
     dist.destroy_process_group()
     return losses, stats
 
@@ -323,6 +331,17 @@ def test_fsdp2_runs_over_lowbit_backend():
     for r in range(2):
         assert got[r][0] == ref[r][0]
     assert got[0][1]["forwarded_calls"] > 0
+
+
+def test_fsdp2_custom_comms_install_and_fall_back_on_cpu():
+    """enable_lowbit_fsdp2 installs one all-gather / reduce-scatter pair per
+    FSDP module; CPU tensors fall back to the group's own collectives, so
+    training matches plain gloo exactly (the fused path is tested on GPUs)."""
+    ref = run_ranks(_w_fsdp2, 2, ("gloo",))
+    got = run_ranks(_w_fsdp2, 2, ("gloo", True))
+    for r in range(2):
+        assert got[r][0] == ref[r][0]
+    assert got[0][1] == {"modules": ["", "0"], "fused": 0}
 
 
 def _w_bucketer(rank, world, bits):

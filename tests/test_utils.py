@@ -99,6 +99,27 @@ def test_tuning_table_thresholds(tmp_path, monkeypatch):
     tuning.load_table.cache_clear()
 
 
+def test_tuning_table_entries(tmp_path, monkeypatch):
+    """Per (world, bits, format) entries: selected by world size, formats
+    mapped to the native codes, missing values as -1."""
+    import json
+
+    from bitscom_b200 import tuning
+
+    f = tmp_path / "t.json"
+    f.write_text(json.dumps({"entries": [
+        {"world": 8, "bits": 4, "fmt": "int", "oneshot_max_packed_bytes": 65536, "ws_min_packed_bytes": 1 << 24},
+        {"world": 8, "bits": 8, "fmt": "e4m3", "oneshot_max_packed_bytes": 131072},
+        {"world": 2, "bits": 2, "fmt": "int", "ws_min_packed_bytes": 0},
+    ]}))
+    monkeypatch.setenv("BITSCOM_TUNING_FILE", str(f))
+    tuning.load_table.cache_clear()
+    assert tuning.entries(8) == [(4, 0, 65536, 1 << 24), (8, 1, 131072, -1)]
+    assert tuning.entries(2) == [(2, 0, -1, 0)]
+    assert tuning.entries(4) == []
+    tuning.load_table.cache_clear()
+
+
 def test_sign_block_model_scale_and_error():
     """CPU model of the sign-magnitude 1-bit format: the block scale is the
     mean |x| (summed in the kernel's order), and on N(0, 1) data one 1-bit

@@ -61,11 +61,14 @@ class Communicator:
     def __init__(self, native, group=None):
         self._c = native
         self.group = group
-        from ..tuning import entries, oneshot_max_bytes
+        from ..tuning import entries, oneshot_max_bytes, schedule_lag
 
         native.set_oneshot_max_bytes(oneshot_max_bytes(native.world))
         for bits, fmt, one, ws in entries(native.world):
             native.set_tuning(bits, fmt, one, ws)
+        lag = schedule_lag(native.world)
+        if lag is not None and "BITSCOM_SCHED_LAG" not in os.environ:
+            native.set_schedule_lag(lag)
 
     # ------------------------------------------------------------------ setup
     @classmethod

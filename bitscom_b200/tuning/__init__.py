@@ -11,8 +11,12 @@ by ``BITSCOM_TUNING_FILE``) with
   packed size from which the warp-specialised kernel runs instead of the
   register kernel; -1 or absent: never).
 
-``BITSCOM_ALGO=oneshot|twoshot`` and ``BITSCOM_KERNEL=ws|reg`` override the
-automatic choices altogether (read by the native communicator).
+* ``schedule_lag``: per world size, the chunk-group lag of the fused
+  kernel's work order (0: phase-major).
+
+``BITSCOM_ALGO=oneshot|twoshot``, ``BITSCOM_KERNEL=ws|reg`` and
+``BITSCOM_SCHED_LAG`` override the automatic choices altogether (read by the
+native communicator).
 """
 
 from __future__ import annotations
@@ -64,3 +68,13 @@ def entries(world: int, path: Optional[str] = None):
         out.append((int(e["bits"]), FMTS[e.get("fmt", "int")], int(e.get("oneshot_max_packed_bytes", -1)),
                     int(e.get("ws_min_packed_bytes", -1))))
     return out
+
+
+def schedule_lag(world: int, path: Optional[str] = None) -> Optional[int]:
+    """Measured schedule lag for ``world`` ranks, or None (keep the default)."""
+    try:
+        table = load_table(path)
+    except (OSError, ValueError):
+        return None
+    v = table.get("schedule_lag", {}).get(str(int(world)))
+    return None if v is None else int(v)

@@ -182,3 +182,29 @@ def test_info_entry_point_runs():
 
     d = info()
     assert d["bitscom_b200"] and "tuning" in d and isinstance(d["devices"], list)
+
+
+def test_tuning_table_crossover_from_sweep_rows():
+    """make_tuning_table: the one-shot threshold is the largest packed size
+    up to which one-shot was never slower (a later one-shot win after a loss
+    does not extend it); always-two-shot formats get 0."""
+    import importlib.util
+    from pathlib import Path
+
+    path = Path(__file__).resolve().parents[1] / "benchmarks" / "make_tuning_table.py"
+    spec = importlib.util.spec_from_file_location("make_tuning_table", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+
+    def row(algo, mb, ms, bits=4, fmt="int", world=8):
+        return {"impl": "ours", "algo": algo, "bits": bits, "fmt": fmt, "world": world,
+                "bytes_fp32": mb << 20, "ms": ms}
+
+    rows = [row("oneshot", 1, 0.01), row("twoshot", 1, 0.02),
+            row("oneshot", 2, 0.02), row("twoshot", 2, 0.02),
+            row("oneshot", 4, 0.05), row("twoshot", 4, 0.03),
+            row("oneshot", 8, 0.04), row("twoshot", 8, 0.05),  # noise after the crossover
+            row("oneshot", 1, 0.03, bits=8, fmt="e4m3"), row("twoshot", 1, 0.02, bits=8, fmt="e4m3"),
+            {"impl": "nccl", "bits": 32, "fmt": "fp32", "world": 8, "bytes_fp32": 1 << 20, "ms": 0.01}]
+    cross = mod.crossover(rows)
+    assert cross == {(8, 4, "int"): (2 << 20) // 4 * 4 // 8, (8, 8, "e4m3"): 0}

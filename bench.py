@@ -61,6 +61,8 @@ def parse():
                    help="broadcast BatchNorm buffers from rank 0 before every forward (DDP's default); off by default "
                         "because the reference's training loop synchronises gradients only")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cudnn-benchmark", action="store_true",
+                   help="both arms: keep cuDNN's heuristic algorithm choice (default: benchmark mode)")
     p.add_argument("--eager", action="store_true",
                    help="our arm: run the step eagerly instead of replaying it as one CUDA graph")
     p.add_argument("--ref-path", choices=["ef", "python"], default="ef",
@@ -72,6 +74,9 @@ def parse():
 # distributed plumbing
 # ----------------------------------------------------------------------------
 def setup(args):
+    # Torch-level setting shared by both arms: cuDNN picks the fastest
+    # convolution algorithms for these fixed shapes during the warm-up steps.
+    torch.backends.cudnn.benchmark = not args.no_cudnn_benchmark
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -429,7 +434,8 @@ def main():
                 "comm": (f"{args.bits}-bit error-feedback low-bit all-reduce, {args.bucket_mb} MB buckets"
                          if args.hook == "lowbit" or args.impl == "reference"
                          else f"fp32 NCCL all-reduce (diagnostic), {args.bucket_mb} MB buckets"),
-                "optimizer": "SGD momentum 0.9",
+                "optimizer": "SGD momentum 0.9 (fused)",
+                "cudnn_benchmark": not args.no_cudnn_benchmark,
                 "buffer_sync": ("DDP broadcast of BatchNorm buffers every forward" if args.broadcast_buffers
                                 else "none (gradients only, as in the reference's loop)"),
                 "l2": f"rotating pool of {POOL} device-resident batches ({POOL * 3} MiB > 126 MiB L2)",

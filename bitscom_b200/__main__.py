@@ -37,6 +37,19 @@ def info() -> dict:
         out["tuning"] = load_table()
     except (OSError, ValueError) as exc:
         out["tuning"] = f"unavailable: {exc!r}"
+    import os
+
+    out["kernel"] = {
+        "variant": os.environ.get("BITSCOM_KERNEL", "auto (register kernel unless a tuning entry selects the "
+                                                     "warp-specialised one)"),
+        "algo": os.environ.get("BITSCOM_ALGO", "auto"),
+        "workspace_mb": int(os.environ.get("BITSCOM_WORKSPACE_MB", "256")),
+    }
+    ref = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref",
+                       "bitscom_b200_install.json")
+    if os.path.exists(ref):
+        with open(ref, encoding="utf-8") as fh:
+            out["reference_build"] = json.load(fh)
     return out
 
 

@@ -420,6 +420,12 @@ __global__ void __launch_bounds__(kThreads, 2) lowbit_coll_kernel(const __grid_c
         const int64_t sub = c * p.sub_per_item + g;
         if (sub >= p.n_sub) break;
         const int64_t off = sub * kSubElems + warp * kBlockElems;
+        // Bulk-prefetch this warp's block of the next sub-chunk into L2 (TMA
+        // engine, no registers held): its loads then wait on L2, not DRAM.
+        if (lane == 0 && g + 1 < p.sub_per_item && off + kSubElems + kBlockElems <= lim) {
+          if (vx) bulk_prefetch_l2(in + base + off + kSubElems, kBlockElems * static_cast<uint32_t>(sizeof(T)));
+          if (has_res && vr) bulk_prefetch_l2(residual + base + off + kSubElems, kBlockElems * static_cast<uint32_t>(sizeof(R)));
+        }
         float v[32];
         load_block<T>(in, base + off, base + lim, vx, lane, v);
         if (has_res) {

@@ -344,6 +344,12 @@ def main():
     xs_dev, ys_dev = xs.cuda(), ys.cuda()
     xs_pin, ys_pin = xs.pin_memory(), ys.pin_memory()
 
+    # Clock samples (nvidia-smi, every 100 ms) from the warm-up steps through
+    # the timed regions: the same workload runs throughout, and a timed
+    # region of a few steps alone can end before the first sample.
+    from bitscom_b200.utils.clocks import ClockSampler
+
+    cs = ClockSampler(list(range(world)) if rank == 0 else [local], period_ms=100).__enter__()
     graph = args.impl == "ours" and not args.eager and args.hook == "lowbit"
     bufs = None
     kernel_ms = None
@@ -384,11 +390,8 @@ def main():
         step(xs_dev[i % POOL], ys_dev[i % POOL])
     barrier_sync(world)
 
-    from bitscom_b200.utils.clocks import ClockSampler
-
     l0 = launches()
-    with ClockSampler(list(range(world)) if rank == 0 else [local]) as cs:
-        ms, _ = timed(step, xs_dev, ys_dev, args.steps, world)
+    ms, _ = timed(step, xs_dev, ys_dev, args.steps, world)
     l1 = launches()
     if per_step_launches is not None:  # replays do not pass through the host
         l1 = l0 + per_step_launches * args.steps
@@ -409,6 +412,7 @@ def main():
         kernel_ms = fused_kernel_ms(step, xs_dev, ys_dev, 5, world)
     identical = replicas_identical(world)
     value = args.batch * world * args.steps / (ms / 1e3)
+    cs.__exit__(None, None, None)
     clocks = cs.summary()
     if rank == 0:
         out = {

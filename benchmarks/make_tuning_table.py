@@ -3,9 +3,11 @@
 Input: JSON documents written by ``benchmarks/allreduce_sweep.py --algos
 oneshot twoshot --out FILE`` (one per world size; any bitwidths and formats).
 For every (world, bits, format) the one-shot threshold is the largest packed
-message size per rank at which one-shot was at least as fast as two-shot,
-provided one-shot also won at every smaller measured size (the crossover);
-a format where two-shot always wins gets threshold 0.  Writes the table
+message size per rank at which one-shot was at least as fast as two-shot and
+above which two-shot won at every measured size (the crossover, read from
+the large end so that one noisy small-size sample does not cut it short); a
+format where two-shot wins at every size gets threshold 0.  When one-shot
+still wins at the largest measured size, that size is the threshold.  Writes the table
 read by ``bitscom_b200.tuning`` (``BITSCOM_TUNING_FILE`` or the shipped
 ``bitscom_b200/tuning/b200.json``), keeping the table's other keys.
 
@@ -33,13 +35,12 @@ def crossover(rows):
     out = {}
     for key, by_size in times.items():
         best = 0
-        for packed in sorted(by_size):
+        for packed in sorted(by_size, reverse=True):
             t = by_size[packed]
             if "oneshot" not in t or "twoshot" not in t:
                 continue
             if t["oneshot"] <= t["twoshot"]:
                 best = packed
-            else:
                 break
         out[key] = best
     return out

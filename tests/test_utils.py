@@ -186,8 +186,9 @@ def test_info_entry_point_runs():
 
 def test_tuning_table_crossover_from_sweep_rows():
     """make_tuning_table: the one-shot threshold is the largest packed size
-    up to which one-shot was never slower (a later one-shot win after a loss
-    does not extend it); always-two-shot formats get 0."""
+    at which one-shot won with two-shot winning at every larger size (an
+    isolated small-size loss does not cut it short); always-two-shot formats
+    get 0."""
     import importlib.util
     from pathlib import Path
 
@@ -200,10 +201,10 @@ def test_tuning_table_crossover_from_sweep_rows():
         return {"impl": "ours", "algo": algo, "bits": bits, "fmt": fmt, "world": world,
                 "bytes_fp32": mb << 20, "ms": ms}
 
-    rows = [row("oneshot", 1, 0.01), row("twoshot", 1, 0.02),
+    rows = [row("oneshot", 1, 0.03), row("twoshot", 1, 0.02),  # a noisy small-size sample
             row("oneshot", 2, 0.02), row("twoshot", 2, 0.02),
             row("oneshot", 4, 0.05), row("twoshot", 4, 0.03),
-            row("oneshot", 8, 0.04), row("twoshot", 8, 0.05),  # noise after the crossover
+            row("oneshot", 8, 0.06), row("twoshot", 8, 0.05),
             row("oneshot", 1, 0.03, bits=8, fmt="e4m3"), row("twoshot", 1, 0.02, bits=8, fmt="e4m3"),
             {"impl": "nccl", "bits": 32, "fmt": "fp32", "world": 8, "bytes_fp32": 1 << 20, "ms": 0.01}]
     cross = mod.crossover(rows)

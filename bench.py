@@ -1,7 +1,7 @@
 """Headline benchmark: DDP training throughput with 4-bit error-feedback
 low-bit gradient all-reduce.
 
-Config: ResNet-18 CIFAR-style (3x3 stem, no max-pool,
+Config (the DDP benchmark configuration named in BASELINE.json): ResNet-18 CIFAR-style (3x3 stem, no max-pool,
 10-way head), DDP with the low-bit comm hook at 4-bit + error feedback, bf16
 autocast, SGD momentum 0.9, synthetic 32x32x3 fp32 images ~N(0,1) with labels
 uniform over 10 classes, batch 256 per GPU, seed 0.  Weak scaling: every GPU

@@ -1,6 +1,6 @@
 """Low-bit all-reduce sweep: fp32-equivalent bus bandwidth vs message size.
 
-per-rank seeded fp32 gradient-like tensors ~N(0, 1e-3)
+The sweep configuration named in BASELINE.json: per-rank seeded fp32 gradient-like tensors ~N(0, 1e-3)
 with 1% outliers ~N(0, 1e-1), sizes 1 KB .. 1 GB in powers of two, bitwidths
 1/2/4/8 (+ fp8 block-scaled), error feedback on, stochastic rounding, at
 2/4/8 GPUs; compared with NCCL fp32 all-reduce and the reference's low-bit

@@ -1,5 +1,5 @@
 """GPT-2 medium, sharded data parallel with low-bit gradient reduce-scatter and
-low-bit parameter all-gather.
+low-bit parameter all-gather (the sharded configuration named in BASELINE.json).
 
 24 layers, d_model 1024, 16 heads, vocab 50257, seq 1024; bf16 autocast; 8-bit
 reduce-scatter of gradients and 8-bit all-gather of parameters with error

@@ -10,7 +10,7 @@ buckets, GradBucketer over LowBitGroup.all_reduce); the no-compression mode
 is a real fp32 all-reduce;
 timing is device-side (CUDA events, max over ranks).
 
-BASELINE config 4 (ResNet-50 ImageNet shape, 2-bit EF + SR, 25 MB buckets,
+The ResNet-50 configuration named in BASELINE.json (ResNet-50 ImageNet shape, 2-bit EF + SR, 25 MB buckets,
 batch 128/GPU):
 
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \
